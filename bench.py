@@ -1,0 +1,403 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 attention-layer forward (x + attention(x)).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0.  A step is one attention-layer forward over
+one batch of the workload (BASELINE config 2 by default: B8 S2048 D1024 H16,
+causal, fp16).  Multi-GPU runs (torchrun, one process per GPU) are weak
+scaling: every rank runs its own batch of the workload, there is no
+collective on the data path, and `value` is the tokens of all ranks divided
+by the slowest rank's device time.
+
+`value` is kernel-only throughput with inputs resident in HBM: each step is
+the three kernels (QKV GEMM, flash attention, out-proj GEMM with the
+residual epilogue) bracketed by CUDA events on the launching stream, and the
+L2 is flushed (a 256 MB write) between steps, outside the events.  `e2e` is
+the same metric through the public module call with the input copied in from
+pinned host memory and the output copied back inside the timed region.
+`--impl reference` times the reference algorithm on the host CPU (the fp32
+restatement in oracle/), the arm the driver compares against.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attention-layer forward tokens/sec and % of tensor-core roofline at 1/2/4/8 B200"
+UNIT = "tokens/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--batch", type=int, default=None, help="override the workload batch")
+    ap.add_argument("--seq", type=int, default=None, help="override the workload seq_len")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- distributed
+def init_dist(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.path is None:
+            return None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except ValueError:
+                pass
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------- peaks
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic(kernel: str, workload: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(workload, {}).get(kernel)
+
+
+# --------------------------------------------------------------------- CPU arm
+def cpu_reference_rate(cfg, seconds: float, seed: int = 1234):
+    """Tokens/s of the reference algorithm (fp32, the oracle restatement of
+    torch_transformer_benchmark.py:85-122 + :140) on the host CPU, timed with
+    perf_counter like the reference's CPU loop (:502-506).  One step = one
+    batch row of the workload (batch rows never interact)."""
+    from oracle import attention_layer_ref, generate_case, make_weights
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x, _ = generate_case(1, cfg.seq_len, cfg.d_model, seed)
+    w = make_weights(cfg.d_model, seed)
+    with torch.inference_mode():
+        attention_layer_ref(x, w, cfg.num_heads, None, cfg.causal)  # warm-up
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            attention_layer_ref(x, w, cfg.num_heads, None, cfg.causal)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds or n >= 200:
+                break
+    return n * cfg.seq_len / el, threads, f"{n} forwards of 1 batch row (S={cfg.seq_len}, D={cfg.d_model}, H={cfg.num_heads}, fp32) in {el:.1f}s"
+
+
+def run_reference(args, cfg):
+    rank, world, _ = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    if rank != 0:
+        return 0
+    per_step = []
+    steps_total = args.warmup + args.steps
+    budget = max(2.0, 120.0 / steps_total)  # whole run within a few minutes
+    from oracle import attention_layer_ref, generate_case, make_weights
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x, _ = generate_case(1, cfg.seq_len, cfg.d_model, 1234)
+    w = make_weights(cfg.d_model, 1234)
+    with torch.inference_mode():
+        for i in range(steps_total):
+            t0 = time.perf_counter()
+            n = 0
+            while True:
+                attention_layer_ref(x, w, cfg.num_heads, None, cfg.causal)
+                n += 1
+                if time.perf_counter() - t0 >= budget:
+                    break
+            el = time.perf_counter() - t0
+            if i >= args.warmup:
+                per_step.append((n * cfg.seq_len, el))
+    tok = sum(t for t, _ in per_step)
+    sec = sum(s for _, s in per_step)
+    value = tok / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec / len(per_step),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, N(0,1) inputs, N(0,0.02) weights)",
+        "config": {"workload": cfg.name, "batch": cfg.batch, "seq_len": cfg.seq_len,
+                   "d_model": cfg.d_model, "heads": cfg.num_heads, "causal": cfg.causal,
+                   "sample": "each step: whole 1-row forwards for ~%.0fs" % budget},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"1 batch row (S={cfg.seq_len}) per forward, fp32, "
+                                   f"{len(per_step)} timed steps"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------- GPU arm
+def run_ours(args, cfg):
+    from oracle import make_weights  # only to seed weights identically to the tests
+    from tiktok_techjam_2026_track3_b200 import B200AttentionLayer, ops
+    from tiktok_techjam_2026_track3_b200 import _lib
+    import ctypes as C
+
+    rank, world, local = init_dist(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    dtype = cfg.torch_dtype
+    B, S, D, H = cfg.batch, cfg.seq_len, cfg.d_model, cfg.num_heads
+    T = B * S
+    layer = B200AttentionLayer(D, H, quant=cfg.quant)
+    layer.load_state_dict(make_weights(D, 1234).state_dict())
+    layer = layer.to(device=dev, dtype=dtype).eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    x = torch.randn(B, S, D, generator=g, device=dev, dtype=dtype) * cfg.input_scale
+    lib = _lib.load()
+    dt = 0 if dtype == torch.float16 else 1
+    status = ops.status_word(dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    # Pre-allocated buffers: the timed step is exactly the three kernels.
+    if cfg.quant == "int8":
+        w8, s8, b32, wo8, so8, bo32 = layer.packed_weights()
+        act8 = torch.empty(T, D, dtype=torch.int8, device=dev)
+        s_tok = torch.empty(T, dtype=torch.float32, device=dev)
+    else:
+        w_qkv, b_qkv, w_o, b_o = layer.packed_weights()
+    qkv = torch.empty(T, 3 * D, dtype=dtype, device=dev)
+    ctx = torch.empty(T, D, dtype=dtype, device=dev)
+    out = torch.empty_like(x)
+
+    def step(ev):
+        rc = 0
+        ev[0].record(stream)
+        if cfg.quant == "int8":
+            rc |= lib.ttj_int8_quant_rows(x.data_ptr(), act8.data_ptr(), s_tok.data_ptr(), T, D, dt, sp)
+            rc |= lib.ttj_int8_linear_fwd(act8.data_ptr(), s_tok.data_ptr(), w8.data_ptr(), s8.data_ptr(),
+                                          b32.data_ptr(), None, None, qkv.data_ptr(), T, 3 * D, D, dt,
+                                          status.data_ptr(), sp)
+        else:
+            rc |= lib.ttj_qkv_proj_fwd(x.data_ptr(), w_qkv.data_ptr(), b_qkv.data_ptr(), qkv.data_ptr(),
+                                       T, D, dt, status.data_ptr(), sp)
+        ev[1].record(stream)
+        rc |= lib.ttj_flash_attn_fwd(qkv.data_ptr(), None, ctx.data_ptr(), B, S, H, D // H,
+                                     int(cfg.causal), dt, status.data_ptr(), sp)
+        ev[2].record(stream)
+        if cfg.quant == "int8":
+            rc |= lib.ttj_int8_quant_rows(ctx.data_ptr(), act8.data_ptr(), s_tok.data_ptr(), T, D, dt, sp)
+            rc |= lib.ttj_int8_linear_fwd(act8.data_ptr(), s_tok.data_ptr(), wo8.data_ptr(), so8.data_ptr(),
+                                          bo32.data_ptr(), x.data_ptr(), None, out.data_ptr(), T, D, D, dt,
+                                          status.data_ptr(), sp)
+        else:
+            rc |= lib.ttj_out_proj_residual_fwd(ctx.data_ptr(), w_o.data_ptr(), b_o.data_ptr(), x.data_ptr(),
+                                                None, out.data_ptr(), T, D, dt, status.data_ptr(), sp)
+        ev[3].record(stream)
+        if rc:
+            raise RuntimeError(f"launch failed: {lib.ttj_last_error().decode()}")
+
+    launches_per_step = 5 if cfg.quant == "int8" else 3
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    warm = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            flush.zero_()
+            step(warm)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        with ClockSampler(dev.index if world == 1 else local) as clk:
+            for i in range(args.steps):
+                flush.zero_()
+                step(evs[i])
+            torch.cuda.synchronize(dev)
+        barrier(world)
+        torch.cuda.synchronize(dev)
+    ops.check_device_status(dev)
+    step_ms = [e[0].elapsed_time(e[3]) for e in evs]
+    qkv_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    attn_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    outp_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    total_ms = max_over_ranks(sum(step_ms), world)
+    ms_per_step = total_ms / args.steps
+    value = world * T * args.steps / (total_ms / 1e3)
+
+    # ---- roofline of the dominant kernel (largest share of the step)
+    from tiktok_techjam_2026_track3_b200.config import attention_flops
+    peaks = measured_peaks()
+    flops_attn = attention_flops(cfg, include_projections=False)
+    flops_qkv = 2.0 * T * D * 3 * D
+    flops_out = 2.0 * T * D * D
+    peak_tf = peaks["bf16_tflops"] * (2.0 if cfg.quant == "int8" else 1.0)
+    kernels = {
+        "qkv_gemm": (statistics.mean(qkv_ms), flops_qkv),
+        "flash_attn": (statistics.mean(attn_ms), flops_attn),
+        "out_proj_residual": (statistics.mean(outp_ms), flops_out),
+    }
+    dom = max(kernels, key=lambda k: kernels[k][0])
+    dom_ms, dom_flops = kernels[dom]
+    achieved = dom_flops / (dom_ms / 1e3) / 1e12
+    layer_tf = attention_flops(cfg) / (ms_per_step / 1e3) / 1e12
+    clocks = clk.summary()
+
+    # ---- e2e through the public module call, pinned host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(x_host.shape, dtype=dtype).pin_memory()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    with torch.inference_mode():
+        for _ in range(max(3, args.warmup)):
+            out_host.copy_(layer(x_host.to(dev, non_blocking=True), None, cfg.causal), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        for i in range(args.steps):
+            flush.zero_()
+            e2e_ev[i][0].record(stream)
+            xd = x_host.to(dev, non_blocking=True)
+            o = layer(xd, None, cfg.causal)
+            out_host.copy_(o, non_blocking=True)
+            e2e_ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_ev), world)
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+    nbytes = x_host.numel() * x_host.element_size()
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": {"float16": "fp16", "bfloat16": "bf16"}[cfg.dtype] + ("+int8" if cfg.quant else ""),
+        "data": "synthetic (seeded; x ~ N(0,1), weights/biases ~ N(0,0.02))",
+        "config": {"workload": cfg.name, "batch_per_gpu": B, "seq_len": S, "d_model": D,
+                   "heads": H, "head_dim": D // H, "causal": cfg.causal, "parallelism": f"dp{world} (batch shards, weak)",
+                   "l2": "flushed between timed steps (256 MB write, outside the events)"},
+        "layer_tflops": layer_tf,
+        "layer_frac_of_peak": layer_tf / peak_tf,
+        "kernels_ms": {k: v[0] for k, v in kernels.items()},
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                     "peak_source": f"{peaks['source']} ({'2x ' if cfg.quant else ''}bf16 dense burst)",
+                     "traffic": ncu_traffic(dom, cfg.name)},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nbytes,
+                "d2h_bytes_per_step": nbytes},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_reference_rate(cfg, args.cpu_sample_seconds)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    from tiktok_techjam_2026_track3_b200.config import PRESETS
+    cfg = PRESETS[args.config]
+    if args.batch:
+        cfg = cfg.with_(batch=args.batch)
+    if args.seq:
+        cfg = cfg.with_(seq_len=args.seq)
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    return run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,100 @@
+"""Flash-attention kernel through the C ABI against the fp32 oracle.
+
+The kernel reads q/k/v head slices from a packed [B,S,3D] buffer; the
+reference computes the same attention from the fp32 upcast of that buffer
+(dense for short sequences, the streamed stripe oracle for long ones)."""
+
+import pytest
+import torch
+
+from oracle import compare_outputs, streamed_attention_ref
+from tiktok_techjam_2026_track3_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+DT = {"fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+def dense_ref(qkv, H, causal, key_mask=None):
+    B, S, D3 = qkv.shape
+    D = D3 // 3
+    hd = D // H
+    q, k, v = (t.float().view(B, S, H, hd).transpose(1, 2) for t in qkv.split(D, -1))
+    s = (q @ k.transpose(-1, -2)) * hd ** -0.5
+    if causal:
+        s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
+    if key_mask is not None:
+        s = s.masked_fill(~key_mask[:, None, None, :], float("-inf"))
+    return (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B, S, D)
+
+
+def make_qkv(B, S, H, hd, dt, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(B, S, 3 * H * hd, generator=g).to(DT[dt]).cuda()
+
+
+CASES = [  # (B, S, H, hd, causal)
+    (1, 1, 1, 64, True), (2, 77, 2, 64, False), (1, 128, 1, 64, True), (2, 200, 4, 64, True),
+    (1, 129, 1, 128, False), (3, 333, 2, 128, True), (1, 1000, 2, 128, False),
+    (2, 2048, 16, 64, True), (1, 4096, 2, 128, True), (2, 1024, 4, 64, False),
+]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B,S,H,hd,causal", CASES)
+def test_flash_matches_dense(dt, B, S, H, hd, causal):
+    qkv = make_qkv(B, S, H, hd, dt, B * 1000 + S + hd)
+    ctx = ops.flash_attn(qkv, H, causal)
+    ref = dense_ref(qkv, H, causal)
+    rep = compare_outputs(ref, ctx.float())
+    assert rep.passed, str(rep)
+    ops.check_device_status(qkv.device)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("kind", ["prefix", "random"])
+@pytest.mark.parametrize("B,S,H,hd,causal", [(3, 200, 2, 64, True), (2, 300, 2, 128, False),
+                                             (2, 1024, 4, 64, True)])
+def test_flash_key_mask(dt, kind, B, S, H, hd, causal):
+    qkv = make_qkv(B, S, H, hd, dt, 77 + S)
+    g = torch.Generator().manual_seed(S)
+    if kind == "prefix":
+        lens = torch.randint(1, S + 1, (B,), generator=g)
+        mask = torch.arange(S)[None, :] < lens[:, None]
+    else:
+        mask = torch.rand(B, S, generator=g) > 0.4
+        mask[:, 0] = True  # every query keeps at least one key
+    mask = mask.cuda()
+    ctx = ops.flash_attn(qkv, H, causal, key_mask=mask)
+    ref = dense_ref(qkv, H, causal, mask)
+    rep = compare_outputs(ref, ctx.float())
+    assert rep.passed, str(rep)
+
+
+@pytest.mark.parametrize("S,H,hd", [(100000, 2, 64), (262144, 1, 128)])
+def test_flash_long_sequence_stripes(S, H, hd):
+    """Long-context shapes (configs 4 and 5 per head): sampled query stripes
+    against the streamed fp32 oracle, including the first and last rows."""
+    qkv = make_qkv(1, S, H, hd, "bf16", S)
+    ctx = ops.flash_attn(qkv, H, True)
+    D = H * hd
+    rows = torch.tensor([0, 1, 127, 128, 4095, S // 3, S // 2 + 17, S - 129, S - 1])
+    for h in range(H):
+        q = qkv[0, :, h * hd:(h + 1) * hd]
+        k = qkv[0, :, D + h * hd:D + (h + 1) * hd]
+        v = qkv[0, :, 2 * D + h * hd:2 * D + (h + 1) * hd]
+        ref = streamed_attention_ref(q[rows.cuda()], k, v, hd ** -0.5, True, q_rows=rows.cuda(),
+                                     k_chunk=16384)
+        got = ctx[0, rows.cuda(), h * hd:(h + 1) * hd].float()
+        rep = compare_outputs(ref, got)
+        assert rep.passed, f"head {h}: {rep}"
+    ops.check_device_status(qkv.device)
+
+
+def test_flash_is_deterministic_and_input_untouched():
+    qkv = make_qkv(2, 512, 4, 64, "fp16", 5)
+    before = qkv.clone()
+    a = ops.flash_attn(qkv, 4, True)
+    b = ops.flash_attn(qkv, 4, True)
+    assert torch.equal(a, b)
+    assert torch.equal(qkv, before)

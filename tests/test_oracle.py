@@ -1,0 +1,131 @@
+"""The oracle against the golden vectors written from the reference's own code.
+
+CPU only.  tests/golden/*.pt were produced by tests/golden/make_golden.py,
+which imports the reference's torch_transformer_benchmark.py and
+Project/kernels/k008_int8_gemm.py unmodified.
+"""
+
+import pytest
+import torch
+
+from oracle import (LayerWeights, attention_layer_ref, attention_layer_streamed_ref,
+                    compare_outputs, generate_case, int8_linear_ref, int_gemm_ref,
+                    quant_rows_ref, quant_weight_ref, split_heads, streamed_attention_ref)
+
+ATTN_FIXTURES = ["cfg1_noncausal", "cfg1_causal", "padded_causal", "ragged_hd128", "tiny_s1"]
+
+
+def load(golden_dir, name):
+    return torch.load(golden_dir / f"{name}.pt", weights_only=False)
+
+
+@pytest.mark.parametrize("name", ATTN_FIXTURES)
+def test_generator_matches_reference(golden_dir, name):
+    fx = load(golden_dir, f"attn_{name}")
+    x, mask = generate_case(fx["batch"], fx["seq_len"], fx["d_model"], fx["seed"],
+                            padding_ratio=fx["padding_ratio"])
+    assert torch.equal(x, fx["x"])
+    assert torch.equal(mask, fx["mask"])
+
+
+@pytest.mark.parametrize("name", ATTN_FIXTURES)
+def test_dense_oracle_matches_reference(golden_dir, name):
+    fx = load(golden_dir, f"attn_{name}")
+    w = LayerWeights.from_state_dict(fx["state_dict"])
+    mask = fx["mask"] if fx["use_mask"] else None
+    out = attention_layer_ref(fx["x"], w, fx["heads"], mask, fx["causal"])
+    torch.testing.assert_close(out, fx["out"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ATTN_FIXTURES)
+def test_streamed_oracle_matches_reference(golden_dir, name):
+    """Streamed (online-softmax) attention equals the reference on every row."""
+    fx = load(golden_dir, f"attn_{name}")
+    w = LayerWeights.from_state_dict(fx["state_dict"])
+    x = fx["x"]
+    B, S, D = x.shape
+    H = fx["heads"]
+    mask = fx["mask"] if fx["use_mask"] else None
+    q = split_heads(torch.nn.functional.linear(x, w.wq, w.bq), H)
+    k = split_heads(torch.nn.functional.linear(x, w.wk, w.bk), H)
+    v = split_heads(torch.nn.functional.linear(x, w.wv, w.bv), H)
+    ctx = torch.empty_like(q)
+    for b in range(B):
+        for h in range(H):
+            ctx[b, h] = streamed_attention_ref(q[b, h], k[b, h], v[b, h], (D // H) ** -0.5,
+                                               fx["causal"], None if mask is None else mask[b],
+                                               k_chunk=32)
+    out = torch.nn.functional.linear(ctx.transpose(1, 2).reshape(B, S, D), w.wo, w.bo)
+    if mask is not None:
+        out = out.masked_fill(~mask[..., None], 0)
+    torch.testing.assert_close(x + out, fx["out"], rtol=1e-5, atol=1e-5)
+
+
+def test_streamed_matches_dense_long():
+    """The long-context checker against dense attention at S up to 1024 (the
+    validation gate the reference applies to its own streamed oracle)."""
+    g = torch.Generator().manual_seed(7)
+    for S, causal in ((1024, True), (700, False)):
+        q, k, v = (torch.randn(S, 64, generator=g) for _ in range(3))
+        dense = torch.softmax(
+            (q @ k.T * 0.125).masked_fill(torch.ones(S, S, dtype=torch.bool).triu(1), float("-inf"))
+            if causal else q @ k.T * 0.125, -1) @ v
+        rows = torch.tensor([0, 1, 127, 128, S // 2, S - 1])
+        got = streamed_attention_ref(q[rows], k, v, 0.125, causal, q_rows=rows, k_chunk=256)
+        torch.testing.assert_close(got, dense[rows], rtol=1e-5, atol=1e-5)
+
+
+def test_sampled_stripe_oracle_matches_dense(golden_dir):
+    fx = load(golden_dir, "attn_cfg1_causal")
+    w = LayerWeights.from_state_dict(fx["state_dict"])
+    x = fx["x"]
+    H = fx["heads"]
+    rows = torch.tensor([0, 5, 64, 127])
+    got = attention_layer_streamed_ref(x, w, H, True, [1], [2], rows, k_chunk=48)
+    q = split_heads(torch.nn.functional.linear(x, w.wq, w.bq), H)
+    k = split_heads(torch.nn.functional.linear(x, w.wk, w.bk), H)
+    v = split_heads(torch.nn.functional.linear(x, w.wv, w.bv), H)
+    s = (q @ k.transpose(-1, -2)) * (x.shape[-1] // H) ** -0.5
+    s = s.masked_fill(torch.ones(128, 128, dtype=torch.bool).triu(1), float("-inf"))
+    dense = torch.softmax(s, -1) @ v
+    torch.testing.assert_close(got[0, 0], dense[1, 2, rows], rtol=1e-5, atol=1e-6)
+
+
+def test_predicate_semantics():
+    ref = torch.tensor([1.0, 0.0, 100.0, float("nan")])
+    assert compare_outputs(ref[:3], ref[:3]).passed
+    # abs-only passes near zero, rel-only passes for large values, OR not sum
+    assert compare_outputs(torch.tensor([0.0]), torch.tensor([0.0019])).passed
+    assert not compare_outputs(torch.tensor([0.0]), torch.tensor([0.0021])).passed
+    assert compare_outputs(torch.tensor([100.0]), torch.tensor([101.9])).passed
+    assert not compare_outputs(torch.tensor([100.0]), torch.tensor([102.1])).passed
+    # isclose would accept atol + rtol*|ref| = 0.002 + 0.02; the OR rule does not
+    assert not compare_outputs(torch.tensor([1.0]), torch.tensor([1.021])).passed
+    assert not compare_outputs(ref, ref).passed  # non-finite fails
+
+
+def test_planted_mistake_is_caught(golden_dir):
+    """A wrong result (planted in the oracle's output, on the CPU) must fail."""
+    fx = load(golden_dir, "attn_cfg1_noncausal")
+    w = LayerWeights.from_state_dict(fx["state_dict"])
+    out = attention_layer_ref(fx["x"], w, fx["heads"], None, False)
+    bad = out.clone()
+    bad[1, 17, 3] += 0.05
+    rep = compare_outputs(fx["out"], bad)
+    assert not rep.passed and rep.failed_elements == 1 and rep.worst_index == (1, 17, 3)
+    # causal vs non-causal confusion is caught too
+    wrong = attention_layer_ref(fx["x"], w, fx["heads"], None, True)
+    assert not compare_outputs(fx["out"], wrong).passed
+
+
+def test_int8_recipe_bit_exact(golden_dir):
+    fx = load(golden_dir, "int8_recipe")
+    a8, s_a = quant_rows_ref(fx["h"])
+    assert torch.equal(a8, fx["a8"])
+    assert torch.equal(s_a, fx["s_a"])
+    w8, s_w = quant_weight_ref(fx["weight"])
+    assert torch.equal(w8, fx["w8"])
+    assert torch.equal(s_w, fx["s_w"])
+    assert torch.equal(int_gemm_ref(a8, w8), fx["acc"])
+    y = int8_linear_ref(fx["h"], w8, s_w, fx["bias"])
+    assert torch.equal(y, fx["y"])
