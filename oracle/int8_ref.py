@@ -32,11 +32,19 @@ __all__ = [
 ]
 
 
+def _c127(like: torch.Tensor) -> torch.Tensor:
+    """127 as a tensor.  Dividing by a tensor keeps the IEEE division the
+    recipe specifies on every device (CUDA torch rewrites division by a Python
+    scalar as a reciprocal multiply, which can differ by one ulp)."""
+    return torch.full_like(like, 127.0)
+
+
 def quant_rows_ref(t: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row (per-token) int8 of an fp32 [N,K] matrix -> (int8 [N,K], scale [N]).
     K8:148-151: clamp the row max before dividing by 127."""
     t = t.float()
-    s = t.abs().amax(dim=-1).clamp(min=1e-6) / 127.0
+    amax = t.abs().amax(dim=-1).clamp(min=1e-6)
+    s = amax / _c127(amax)
     q = torch.round(t / s[:, None]).to(torch.int8)
     return q, s
 
@@ -47,7 +55,8 @@ def quant_weight_ref(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     (out, in) row-major here (K-major for the GEMM); K8 transposes it only
     because ``torch._int_mm`` wants [K, N]."""
     w = w.float()
-    s = (w.abs().amax(dim=1) / 127.0).clamp(min=1e-8)
+    amax = w.abs().amax(dim=1)
+    s = (amax / _c127(amax)).clamp(min=1e-8)
     q = torch.round(w / s[:, None]).to(torch.int8)
     return q, s
 

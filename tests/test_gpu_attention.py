@@ -15,7 +15,10 @@ pytestmark = pytest.mark.gpu
 DT = {"fp16": torch.float16, "bf16": torch.bfloat16}
 
 
-def dense_ref(qkv, H, causal, key_mask=None):
+def dense_ref(qkv, H, causal, key_mask=None, probs_dtype=None):
+    """fp32 attention from the packed buffer.  probs_dtype rounds the
+    normalised probabilities the way the reference does in a 16-bit run
+    (``.to(dtype=x.dtype)``, torch_transformer_benchmark.py:111)."""
     B, S, D3 = qkv.shape
     D = D3 // 3
     hd = D // H
@@ -25,7 +28,30 @@ def dense_ref(qkv, H, causal, key_mask=None):
         s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
     if key_mask is not None:
         s = s.masked_fill(~key_mask[:, None, None, :], float("-inf"))
-    return (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B, S, D)
+    p = torch.softmax(s, -1)
+    if probs_dtype is not None:
+        p = p.to(probs_dtype).float()
+    return (p @ v).transpose(1, 2).reshape(B, S, D)
+
+
+def check_ctx(qkv, H, causal, ctx, key_mask=None):
+    """fp16: the reference predicate (abs 2e-3 OR rel 2e-2) against fp32.
+    bf16: bf16 keeps 8 significant bits, so rounding each probability costs up
+    to 2^-9 of it and a context entry can move by ~2^-9 * max|v| (~1e-2 for
+    the N(0,1) values used here) -- the reference's own bf16 run has the same
+    error.  The gate is therefore: within abs 1e-2 OR rel 2e-2 of fp32, and no
+    worse than twice the reference-style rounding error (+1e-3)."""
+    ref = dense_ref(qkv, H, causal, key_mask)
+    if qkv.dtype == torch.float16:
+        rep = compare_outputs(ref, ctx.float())
+        assert rep.passed, str(rep)
+        return
+    rep = compare_outputs(ref, ctx.float(), atol=1e-2)
+    assert rep.passed, str(rep)
+    ref_style = dense_ref(qkv, H, causal, key_mask, probs_dtype=torch.bfloat16).to(torch.bfloat16)
+    err_ours = float((ctx.float() - ref).abs().max())
+    err_refstyle = float((ref_style.float() - ref).abs().max())
+    assert err_ours <= 2 * err_refstyle + 1e-3, (err_ours, err_refstyle)
 
 
 def make_qkv(B, S, H, hd, dt, seed):
@@ -45,9 +71,7 @@ CASES = [  # (B, S, H, hd, causal)
 def test_flash_matches_dense(dt, B, S, H, hd, causal):
     qkv = make_qkv(B, S, H, hd, dt, B * 1000 + S + hd)
     ctx = ops.flash_attn(qkv, H, causal)
-    ref = dense_ref(qkv, H, causal)
-    rep = compare_outputs(ref, ctx.float())
-    assert rep.passed, str(rep)
+    check_ctx(qkv, H, causal, ctx)
     ops.check_device_status(qkv.device)
 
 
@@ -66,9 +90,7 @@ def test_flash_key_mask(dt, kind, B, S, H, hd, causal):
         mask[:, 0] = True  # every query keeps at least one key
     mask = mask.cuda()
     ctx = ops.flash_attn(qkv, H, causal, key_mask=mask)
-    ref = dense_ref(qkv, H, causal, mask)
-    rep = compare_outputs(ref, ctx.float())
-    assert rep.passed, str(rep)
+    check_ctx(qkv, H, causal, ctx, mask)
 
 
 @pytest.mark.parametrize("S,H,hd", [(100000, 2, 64), (262144, 1, 128)])
@@ -86,7 +108,7 @@ def test_flash_long_sequence_stripes(S, H, hd):
         ref = streamed_attention_ref(q[rows.cuda()], k, v, hd ** -0.5, True, q_rows=rows.cuda(),
                                      k_chunk=16384)
         got = ctx[0, rows.cuda(), h * hd:(h + 1) * hd].float()
-        rep = compare_outputs(ref, got)
+        rep = compare_outputs(ref, got, atol=1e-2)  # bf16 probabilities, see check_ctx
         assert rep.passed, f"head {h}: {rep}"
     ops.check_device_status(qkv.device)
 

@@ -1,36 +1,79 @@
-"""W8A8 attention layer (BASELINE config 3 recipe) against the integer/fp32
-oracle of the same recipe (Project/kernels/k008_int8_gemm.py:148-185).
+"""W8A8 attention layer (BASELINE config 3 recipe) against the integer oracle
+of the same recipe (Project/kernels/k008_int8_gemm.py:148-185), stage by stage.
 
-Against the non-quantised fp32 layer int8 is NOT expected to pass the
-2e-3 / 2% predicate (the reference measured ~3.5e-2 max error at d=1024,
-Project/research/quantization-tolerance.md:8-10); that number is reported,
-not gated on."""
+Why stagewise: per-token int8 quantisation of the attention context turns
+any difference in the context below one quantisation step into a flipped
+rounding, so an end-to-end comparison against a recipe evaluated with fp32
+attention mostly measures bf16-vs-fp32 attention, amplified.  The integer
+stages are therefore checked bit for bit given identical inputs, attention is
+checked against fp32 within bf16 tolerance, and the end-to-end distance is
+reported with a loose bound.  Against the non-quantised fp32 layer int8 is
+not expected to pass 2e-3 / 2% (the reference measured ~3.5e-2 max error at
+d=1024, Project/research/quantization-tolerance.md:8-10)."""
 
 import pytest
 import torch
 
-from oracle import (attention_layer_ref, compare_outputs, generate_case, int8_attention_layer_ref,
-                    make_weights)
+from oracle import (LayerWeights, attention_layer_ref, compare_outputs, generate_case,
+                    int8_attention_layer_ref, int8_linear_ref, make_weights)
 from tiktok_techjam_2026_track3_b200 import B200AttentionLayer, ops
 
 pytestmark = pytest.mark.gpu
 
+CASES = [(2, 512, 1024, 8, True), (1, 1000, 512, 4, False), (1, 4096, 4096, 32, True)]
 
-@pytest.mark.parametrize("B,S,D,H,causal", [(2, 512, 1024, 8, True), (1, 1000, 512, 4, False),
-                                            (1, 4096, 4096, 32, True)])
-def test_int8_layer_matches_recipe(B, S, D, H, causal):
+
+def _attn_fp32(qkv, H, causal):
+    B, S, D3 = qkv.shape
+    D = D3 // 3
+    hd = D // H
+    q, k, v = (t.float().view(B, S, H, hd).transpose(1, 2) for t in qkv.split(D, -1))
+    s = (q @ k.transpose(-1, -2)) * hd ** -0.5
+    if causal:
+        s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
+    return (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B, S, D)
+
+
+@pytest.mark.parametrize("B,S,D,H,causal", CASES)
+def test_int8_layer_stagewise(B, S, D, H, causal):
     x, _ = generate_case(B, S, D, 1234, dtype=torch.bfloat16)
+    x = x.cuda()
     w = make_weights(D, 1234)
     layer = B200AttentionLayer(D, H, quant="int8")
     layer.load_state_dict(w.state_dict())
     layer = layer.to(device="cuda", dtype=torch.bfloat16).eval()
-    with torch.inference_mode():
-        out = layer(x.cuda(), None, causal)
+    w8, s8, b32, wo8, so8, bo32 = layer.packed_weights()
     wb = w.to(dtype=torch.bfloat16).to(dtype=torch.float32, device="cuda")
-    ref = int8_attention_layer_ref(x.cuda(), wb, H, causal, round_to=torch.bfloat16)
-    rep = compare_outputs(ref, out.float())
-    assert rep.passed, str(rep)
-    ops.check_device_status(out.device)
-    # informational: distance to the non-quantised layer
-    full = attention_layer_ref(x.cuda(), wb, H, None, causal, batch_chunk=1)
-    print("int8 vs fp32 layer:", compare_outputs(full, out.float()))
+    T = B * S
+    with torch.inference_mode():
+        out = layer(x, None, causal)
+        # the same pipeline stage by stage through the C ABI
+        a8, s_a = ops.int8_quant_rows(x.view(T, D))
+        qkv = ops.int8_linear(a8, s_a, w8, s8, b32, torch.bfloat16).view(B, S, 3 * D)
+        ctx = ops.flash_attn(qkv, H, causal)
+        c8, s_c = ops.int8_quant_rows(ctx.view(T, D))
+        staged = ops.int8_linear(c8, s_c, wo8, so8, bo32, torch.bfloat16,
+                                 residual=x.view(T, D)).view(B, S, D)
+    ops.check_device_status(x.device)
+    # 0. the layer call is exactly the staged composition
+    assert torch.equal(out, staged)
+    # 1. QKV stage: bit-exact against the recipe (quantiser, int32 GEMM, dequant order)
+    wqkv = torch.cat([wb.wq, wb.wk, wb.wv], 0)
+    bqkv = torch.cat([wb.bq, wb.bk, wb.bv], 0)
+    from oracle import quant_weight_ref
+    wq8_ref, sq_ref = quant_weight_ref(wqkv)
+    assert torch.equal(w8, wq8_ref) and torch.equal(s8, sq_ref)
+    qkv_ref = int8_linear_ref(x.view(T, D).float(), wq8_ref, sq_ref, bqkv).to(torch.bfloat16)
+    assert torch.equal(qkv.view(T, 3 * D), qkv_ref)
+    # 2. attention stage against fp32 on the same qkv (bf16 probabilities: abs 1e-2)
+    rep = compare_outputs(_attn_fp32(qkv, H, causal), ctx.float(), atol=1e-2)
+    assert rep.passed, f"attention stage: {rep}"
+    # 3. out-proj stage given our ctx: bit-exact against the recipe + residual
+    wo8_ref, so_ref = quant_weight_ref(wb.wo)
+    out_ref = (x.view(T, D).float() + int8_linear_ref(ctx.view(T, D).float(), wo8_ref, so_ref, wb.bo))
+    assert torch.equal(out.view(T, D), out_ref.to(torch.bfloat16))
+    # end to end (reported): vs the recipe with fp32 attention, and vs the fp32 layer
+    e2e_recipe = compare_outputs(int8_attention_layer_ref(x, wb, H, causal), out.float())
+    e2e_fp32 = compare_outputs(attention_layer_ref(x, wb, H, None, causal, batch_chunk=1), out.float())
+    print(f"\nint8 B{B} S{S} D{D}: vs recipe(fp32 attn) {e2e_recipe}; vs fp32 layer {e2e_fp32}")
+    assert e2e_recipe.max_abs_error < 0.1 and e2e_recipe.mean_abs_error < 5e-3

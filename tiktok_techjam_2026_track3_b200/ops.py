@@ -264,6 +264,10 @@ def quantize_weight(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     (Project/kernels/k008_int8_gemm.py:154-158).  Runs as torch ops on the
     weights' device; it is set-up, not part of the timed forward."""
     wf = w.float()
-    s = (wf.abs().amax(dim=1) / 127.0).clamp(min=1e-8)
+    amax = wf.abs().amax(dim=1)
+    # Divide by a tensor, not a Python scalar: CUDA torch turns a scalar
+    # divisor into a reciprocal multiply, which is not the recipe's IEEE
+    # division and can move the scale by one ulp.
+    s = (amax / torch.full_like(amax, 127.0)).clamp(min=1e-8)
     q = torch.round(wf / s[:, None]).to(torch.int8)
     return q.contiguous(), s.contiguous()
