@@ -157,6 +157,22 @@ size_t ttj_attn_layer_workspace_size(int64_t batch, int64_t seq_len, int64_t d_m
  */
 int ttj_attn_layer_fwd(const ttj_attn_layer_args* args, ttj_stream_t stream);
 
+/*
+ * The same layer for callers that cannot allocate device memory (a host
+ * runtime that owns all device allocations, or one that must not grow its
+ * footprint after start-up): identical kernels and results, but the qkv and
+ * context intermediates live in a fixed 32 MiB array in device memory owned
+ * by the library, so args->workspace / workspace_bytes are ignored.
+ * No counterpart in the reference (its layer always allocates through torch).
+ * Limit: layers whose ttj_attn_layer_workspace_size() exceeds 32 MiB
+ * (33554432 bytes) are rejected with TTJ_ERR_WORKSPACE.  Calls no allocator.
+ * One array per GPU, shared by every call: calls that overlap on the same GPU
+ * race; calls ordered on one stream are safe.  The first call on a device
+ * looks up the array's address with that device current; make it before any
+ * stream capture.  Every GPU that loads the library holds the array until exit.
+ */
+int ttj_attn_layer_fwd_noalloc(const ttj_attn_layer_args* args, ttj_stream_t stream);
+
 /* ------------------------------------------------------------------ int8 */
 
 /*

@@ -27,7 +27,7 @@ EXPORTED_SYMBOLS = (
     "ttj_version", "ttj_status_string", "ttj_last_error", "ttj_read_status",
     "ttj_selftest_wait_timeout",
     "ttj_linear_fwd", "ttj_qkv_proj_fwd", "ttj_flash_attn_fwd", "ttj_out_proj_residual_fwd",
-    "ttj_attn_layer_workspace_size", "ttj_attn_layer_fwd",
+    "ttj_attn_layer_workspace_size", "ttj_attn_layer_fwd", "ttj_attn_layer_fwd_noalloc",
     "ttj_int8_quant_rows", "ttj_int8_gemm_s32", "ttj_int8_linear_fwd",
     "ttj_int8_attn_layer_workspace_size", "ttj_int8_attn_layer_fwd",
 )
@@ -72,6 +72,7 @@ _SIGNATURES = {
     "ttj_out_proj_residual_fwd": (ci, [vp, vp, vp, vp, vp, vp, i64, i64, ci, vp, vp]),
     "ttj_attn_layer_workspace_size": (C.c_size_t, [i64, i64, i64, ci]),
     "ttj_attn_layer_fwd": (ci, [C.POINTER(AttnLayerArgs), vp]),
+    "ttj_attn_layer_fwd_noalloc": (ci, [C.POINTER(AttnLayerArgs), vp]),
     "ttj_int8_quant_rows": (ci, [vp, vp, vp, i64, i64, ci, vp]),
     "ttj_int8_gemm_s32": (ci, [vp, vp, vp, i64, i64, i64, vp, vp]),
     "ttj_int8_linear_fwd": (ci, [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, ci, vp, vp]),
