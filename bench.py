@@ -26,9 +26,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -53,6 +51,8 @@ def parse_args():
     ap.add_argument("--seq", type=int, default=None, help="override the workload seq_len")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=15.0)
+    ap.add_argument("--spinup-seconds", type=float, default=0.5,
+                    help="untimed work after warm-up so clocks leave idle (0 under a profiler)")
     return ap.parse_args()
 
 
@@ -86,58 +86,77 @@ def max_over_ranks(v: float, world: int) -> float:
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML, read
+    only, every ~2 ms in a background thread for the duration of the timed
+    region (nvidia-smi's process start-up alone is longer than a short timed
+    region)."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._handle = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            props = torch.cuda.get_device_properties(device)
+            bus = getattr(props, "pci_bus_id", None)
+            handle = None
+            if bus is not None:
+                dom = getattr(props, "pci_domain_id", 0)
+                dev_id = getattr(props, "pci_device_id", 0)
+                try:
+                    handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev_id:02x}.0")
+                except Exception:
+                    handle = None
+            if handle is None and pynvml.nvmlDeviceGetCount() == 1:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(0)
+            self._handle = handle
+            if handle is not None:
+                self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._handle = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        if self._handle is not None:
+            import threading
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or self.path is None:
+        if not self.samples:
             return None
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append(parts)
-            except ValueError:
-                pass
-        os.unlink(self.path)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+        mhz = [m for m, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = sorted(n for b, n in self.REASONS.items() if bits & b)
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz), "source": "nvml"}
 
 
 # --------------------------------------------------------------------- peaks
@@ -295,10 +314,16 @@ def run_ours(args, cfg):
         for _ in range(args.warmup):
             flush.zero_()
             step(warm)
+        # Untimed spin-up so SM clocks have left idle before timing starts.
+        t_spin = time.perf_counter()
+        while time.perf_counter() - t_spin < args.spinup_seconds:
+            for _ in range(20):
+                step(warm)
+            torch.cuda.synchronize(dev)
         torch.cuda.synchronize(dev)
         barrier(world)
         torch.cuda.synchronize(dev)
-        with ClockSampler(dev.index if world == 1 else local) as clk:
+        with ClockSampler(dev) as clk:
             for i in range(args.steps):
                 flush.zero_()
                 step(evs[i])

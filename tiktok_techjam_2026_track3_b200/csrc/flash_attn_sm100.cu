@@ -1,52 +1,63 @@
-// Flash-attention forward for sm_100a: one CTA per (128-query tile, batch, head).
+// Flash-attention forward for sm_100a (persistent, two query tiles per work item).
 //
 // Q, K and V are read straight from the packed projection buffer qkv[B,S,3D]
 // through one 3-D TMA descriptor (dims 3D x S x B, box 64 x 128 x 1, 128-byte
-// swizzle), so the reference's head split (.view/.transpose/.contiguous) is a
+// swizzle): the reference's head split (.view/.transpose/.contiguous) becomes a
 // coordinate choice, and rows past S arrive as zeros.
 //
-// Roles (256 threads):
-//   warp 0      TMA: Q once, then K_j / V_j tiles into KV_STAGES-deep rings
-//   warp 1      MMA: S_j = Q K_j^T into TMEM (two S buffers, so QK_{j+1}
-//               runs while softmax works on S_j), then O += P_j V_j with P
-//               read from TMEM (tcgen05 "ts" form) and V from shared memory
-//   warps 4..7  softmax: thread r owns query row r; loads its S row from
-//               TMEM, masks, updates the running max / sum in fp32, writes P
-//               (rounded to the input dtype) back to TMEM, rescales its O row
-//               when the max grew, and finally normalises O and stores the
-//               context row into ctx[B,S,D] at the head's columns (head merge).
+// Work item = (batch, head, 256 consecutive queries) = two 128-row query tiles
+// A and B that share every K/V tile.  One CTA per SM loops over work items,
+// heaviest (longest causal key range) first.
 //
-// TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+HD).
+// Roles (352 threads = 11 warps):
+//   warp 0       TMA: K_j / V_j tiles into KV_STAGES-deep rings, item after item
+//   warp 1       MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j
+//                with P read from TMEM (tcgen05 "ts" form)
+//   warp 2       TMA: the two Q tiles of each work item
+//   warps 3..6   softmax for tile A, warps 7..10 for tile B: thread = query row;
+//                load the S row from TMEM, mask, online softmax in fp32 with a
+//                lazily moved row max, write P (input dtype) back over S, rescale
+//                its O row when the max moved, and at the end normalise O and
+//                store the context row at the head's columns of ctx[B,S,D].
+// The two softmax warpgroups run on different tiles, so the tensor core works on
+// one tile while the other tile's exponentials are computed.
+//
+// MMA issue order per tile t and key tile j:  PV_t(j-1), QK_t(j), commit s_full_t.
+// tcgen05.commit arrives only when EVERY earlier MMA of the issuing thread has
+// completed, so "S_t(j) is ready" also means "P_t(j-1) has been consumed and O_t
+// holds P_t(0..j-1) V": the softmax may then overwrite S_t with P_t(j) and rescale
+// O_t without further barriers.
+//
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,256+HD) O_B [256+HD,256+2HD);
+// P_t (16-bit, two per column) overwrites the first 64 columns of S_t.
 #include "sm100_ptx.cuh"
 #include "ttj_internal.h"
 
 namespace ttj {
 namespace {
 
-constexpr int kBM = 128;     // queries per CTA
+constexpr int kBM = 128;     // queries per tile
 constexpr int kBN = 128;     // keys per KV tile
 constexpr int kChunkBytes = 128 * 128;  // one [128 rows][64 cols] 16-bit swizzled box
-
-constexpr uint32_t kColS = 0;
-constexpr uint32_t kColP = 256;
-constexpr uint32_t kColO = 384;
+constexpr int kThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 
 struct AttnParams {
   void* ctx;
   const uint8_t* key_mask;
   int B, S, H, D;
-  int num_q_tiles;
+  int num_pairs;     // ceil(S / 256)
+  int num_items;     // B * H * num_pairs
   float scale_log2;  // head_dim^-0.5 * log2(e)
   int* status;
 };
 
 template <int HD>
 struct AttnSmem {
-  static constexpr int kStages = HD == 64 ? 3 : 2;
+  static constexpr int kStages = HD == 64 ? 4 : 2;
   static constexpr int kTileBytes = HD * 2 * 128;  // 128 rows x HD x 2 bytes
-  static constexpr int kQOff = 0;
-  static constexpr int kKOff = kTileBytes;
+  static constexpr int kQOff = 0;                   // Q_A, Q_B
+  static constexpr int kKOff = 2 * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kTotal = 1024 + kBarOff + 512;
@@ -58,8 +69,32 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Decode work item -> (b, h, pair).  Causal items are ordered by decreasing
+// pair index (longest key range first) so static striding balances the SMs.
+struct Item {
+  int b, h, pair;
+};
+template <bool CAUSAL>
+__device__ __forceinline__ Item decode_item(int item, const AttnParams& p) {
+  const int bh_count = p.B * p.H;
+  const int round = item / bh_count;
+  const int bh = item - round * bh_count;
+  Item it;
+  it.pair = CAUSAL ? p.num_pairs - 1 - round : round;
+  it.b = bh / p.H;
+  it.h = bh - it.b * p.H;
+  return it;
+}
+
+// Number of key tiles tile `t` (0 = A, 1 = B) of a pair attends to.
+template <bool CAUSAL>
+__device__ __forceinline__ int kv_tiles(int pair, int t, int S) {
+  const int total = (S + kBN - 1) / kBN;
+  return CAUSAL ? min(2 * pair + 1 + t, total) : total;
+}
+
 template <typename T, int HD, bool CAUSAL>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   using L = AttnSmem<HD>;
   constexpr int ST = L::kStages;
@@ -67,6 +102,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdescQK = idesc_f16(kBM, kBN, kBf16, 0);
   constexpr uint32_t kIdescPV = idesc_f16(kBM, HD, kBf16, 1);
+  constexpr uint32_t kColO = 256;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -75,43 +111,36 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + ST;
-  uint64_t* v_full = k_empty + ST;
-  uint64_t* v_empty = v_full + ST;
-  uint64_t* s_full = v_empty + ST;   // [2]
-  uint64_t* s_free = s_full + 2;     // [2]
-  uint64_t* p_full = s_free + 2;     // [2]
-  uint64_t* o_done = p_full + 2;     // [1] one phase per completed P.V
-  uint64_t* drain = o_done + 1;
+  uint64_t* q_full = bars;              // [1]
+  uint64_t* q_empty = q_full + 1;       // [1]
+  uint64_t* k_full = q_empty + 1;       // [ST]
+  uint64_t* k_empty = k_full + ST;      // [ST]
+  uint64_t* v_full = k_empty + ST;      // [ST]
+  uint64_t* v_empty = v_full + ST;      // [ST]
+  uint64_t* s_full = v_empty + ST;      // [2] per tile
+  uint64_t* p_full = s_full + 2;        // [2] per tile
+  uint64_t* o_final = p_full + 2;       // [2] per tile
+  uint64_t* drain = o_final + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
-  const int b = bh / p.H;
-  const int h = bh - b * p.H;
-  const int qt = p.num_q_tiles - 1 - (int)blockIdx.y;  // heaviest causal tiles first
-  const int q0 = qt * kBM;
-  const int kv_tiles_total = (p.S + kBN - 1) / kBN;
-  const int n_kv = CAUSAL ? min(qt + 1, kv_tiles_total) : kv_tiles_total;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&p_full[i], 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_final[t], 1);
     }
-    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -127,171 +156,235 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ K/V producer
     if (lane == 0) {
       tma_prefetch_desc(&tm);
-      const int xq = h * HD, xk = p.D + h * HD, xv = 2 * p.D + h * HD;
-      mbar_arrive_expect_tx(q_full, L::kTileBytes);
-      for (int c = 0; c < kChunks; ++c) tma_load_3d(sQ + c * kChunkBytes, &tm, q_full, xq + 64 * c, q0, b);
+      int kv = 0;  // running K/V tile counter across items
       bool ok = true;
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
-        for (int c = 0; c < kChunks; ++c)
-          tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, b);
-        if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
-        for (int c = 0; c < kChunks; ++c)
-          tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, b);
+      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
+        const Item it = decode_item<CAUSAL>(item, p);
+        const int n_kv = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+        const int xk = p.D + it.h * HD, xv = 2 * p.D + it.h * HD;
+        for (int j = 0; j < n_kv; ++j, ++kv) {
+          const int st = kv % ST;
+          const uint32_t ph = (kv / ST) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, it.b);
+          if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, it.b);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ Q producer
+    if (lane == 0) {
+      int k = 0;
+      for (int item = blockIdx.x; item < p.num_items; item += gridDim.x, ++k) {
+        const Item it = decode_item<CAUSAL>(item, p);
+        if (!mbar_wait(q_empty, (k & 1) ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, 2 * L::kTileBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sQ + t * L::kTileBytes + c * kChunkBytes, &tm, q_full, it.h * HD + 64 * c,
+                        it.pair * 2 * kBM + t * kBM, it.b);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutTmaFull, abort_flag);
-      const uint32_t q_addr = smem_u32(sQ);
-      auto issue_qk = [&](int j) -> bool {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, p.status, kDevTimeoutSoftmax, abort_flag))
-          return false;
-        tc_fence_after();
+      int kv = 0, k = 0;
+      uint32_t pf_phase[2] = {0u, 0u};
+      bool ok = true;
+      auto qk = [&](int t, int st) {
+        const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
         const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem + kColS + sb * 128, smem_desc_sw128(q_addr + off, 16, 1024),
+          umma_f16_ss(tmem + t * 128, smem_desc_sw128(q_addr + off, 16, 1024),
                       smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[sb]);
-        umma_commit(&k_empty[st]);
-        return true;
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        const int pb = j & 1;
-        if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) return false;
-        if (!mbar_wait(&p_full[pb], (j >> 1) & 1, p.status, kDevTimeoutSoftmax, abort_flag)) return false;
-        tc_fence_after();
+      auto pv = [&](int t, int st, bool accumulate) {
         const uint32_t v_addr = smem_u32(sV + st * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           // V is MN-major: 16 keys = 16 rows of 128 bytes; next 64-column chunk at +16 KB.
-          umma_f16_ts(tmem + kColO, tmem + kColP + pb * 64 + kk * 8,
+          umma_f16_ts(tmem + kColO + t * HD, tmem + t * 128 + kk * 8,
                       smem_desc_sw128(v_addr + kk * 16 * 128, kChunkBytes, 1024), kIdescPV,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+                      (accumulate || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&v_empty[st]);
-        umma_commit(o_done);
-        return true;
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv && !issue_qk(j + 1)) break;
-        if (!issue_pv(j)) break;
+      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++k) {
+        const Item it = decode_item<CAUSAL>(item, p);
+        const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
+        const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);  // n_b >= n_a
+        if (!mbar_wait(q_full, k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+        const int kv0 = kv;
+        // prologue: S_A(0), S_B(0)
+        {
+          const int st = kv0 % ST;
+          if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+          tc_fence_after();
+          qk(0, st);
+          umma_commit(&s_full[0]);
+          qk(1, st);
+          umma_commit(&s_full[1]);
+          umma_commit(&k_empty[st]);
+        }
+        for (int j = 0; j < n_b; ++j) {
+          const int st = (kv0 + j) % ST;
+          const uint32_t ph = ((kv0 + j) / ST) & 1;
+          const int st_n = (kv0 + j + 1) % ST;
+          const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
+          const bool next_b = j + 1 < n_b;
+          if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+          if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+          if (j < n_a) {
+            if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            pf_phase[0] ^= 1u;
+            tc_fence_after();
+            pv(0, st, j > 0);
+            if (j + 1 < n_a) {
+              qk(0, st_n);
+              umma_commit(&s_full[0]);
+            } else {
+              umma_commit(&o_final[0]);
+            }
+          }
+          if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+          pf_phase[1] ^= 1u;
+          tc_fence_after();
+          pv(1, st, j > 0);
+          umma_commit(&v_empty[st]);
+          if (next_b) {
+            qk(1, st_n);
+            umma_commit(&s_full[1]);
+            umma_commit(&k_empty[st_n]);
+          } else {
+            umma_commit(&o_final[1]);
+          }
+        }
+        kv = kv0 + n_b;
+        umma_commit(q_empty);  // every QK of this item has completed
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.status, kDevTimeoutSoftmax, nullptr);
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------ softmax
-    const int lg = warp & 3;             // TMEM lane quarter
+  } else if (warp >= 3) {
+    // ------------------------------------------------------------ softmax (tile A or B)
+    const int t = warp >= 7 ? 1 : 0;
+    const int lg = warp & 3;             // TMEM lane quarter of this warp
     const int r = lg * 32 + lane;        // query row within the tile
-    const int q_row = q0 + r;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(lg * 32) << 16);
-    const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)b * p.S : nullptr;
-    float m_run = -INFINITY;  // running max, log2 domain
-    float l_run = 0.f;        // running sum of P (fp32, before rounding)
+    const uint32_t t_s = t_lane + t * 128;
+    const uint32_t t_o = t_lane + kColO + t * HD;
+    uint32_t sf_phase = 0, of_phase = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld32(t_lane + kColS + sb * 128 + c * 32, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(u[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-
-      const int k0 = j * kBN;
-      const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && k0 + kBN - 1 > q0) || kmask != nullptr;
-      if (need_mask) {
-        // Validity bits for the tile's 128 keys, built cooperatively: lane l
-        // reads keys l, l+32, l+64, l+96 and one ballot per group of 32.
-        uint32_t vbits[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int key = k0 + g * 32 + lane;
-          bool v = key < p.S;
-          if (v && kmask != nullptr) v = kmask[key] != 0;
-          vbits[g] = __ballot_sync(0xffffffffu, v);
-        }
-#pragma unroll
-        for (int i = 0; i < kBN; ++i) {
-          bool v = (vbits[i >> 5] >> (i & 31)) & 1u;
-          if (CAUSAL) v = v && (k0 + i <= q_row);
-          s[i] = v ? s[i] : -INFINITY;
-        }
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < kBN; ++i) mx = fmaxf(mx, s[i]);
-      const float m_new = fmaxf(m_run, mx * p.scale_log2);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = fast_exp2(m_run - m_use);  // 0 when m_run = -inf
-      float sum = 0.f;
-      const uint32_t t_p = t_lane + kColP + sb * 64;
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float e0 = fast_exp2(fmaf(s[c * 32 + 2 * i], p.scale_log2, -m_use));
-          const float e1 = fast_exp2(fmaf(s[c * 32 + 2 * i + 1], p.scale_log2, -m_use));
-          sum += e0 + e1;
-          pk[i] = Pack<T>::two(e0, e1);
-        }
-        tmem_st16(t_p + c * 16, pk);
-      }
-      l_run = l_run * alpha + sum;
-      // O may only be rescaled once P_{j-1} V_{j-1} has landed.
-      if (j > 0) {
-        if (!mbar_wait_warp(o_done, (j - 1) & 1, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+    for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
+      const Item it = decode_item<CAUSAL>(item, p);
+      const int n_kv = kv_tiles<CAUSAL>(it.pair, t, p.S);
+      const int q0 = it.pair * 2 * kBM + t * kBM;
+      const int q_row = q0 + r;
+      const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
+      float m_run = -INFINITY;  // exponent reference (log2 units), moved lazily
+      float l_run = 0.f;        // running sum of P in fp32
+      for (int j = 0; j < n_kv; ++j) {
+        if (!mbar_wait_warp(&s_full[t], sf_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+        sf_phase ^= 1u;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        float s[kBN];
+        {
+          uint32_t u[kBN];
+          tmem_ld128(t_s, u);
+#pragma unroll
+          for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(u[i]);
+        }
+        const int k0 = j * kBN;
+        const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && k0 + kBN - 1 > q0) || kmask != nullptr;
+        if (need_mask) {
+          // Validity bits for the tile's keys, built cooperatively: lane l reads
+          // keys l, l+32, l+64, l+96, one ballot per group of 32.
+          uint32_t vbits[4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int key = k0 + g * 32 + lane;
+            bool v = key < p.S;
+            if (v && kmask != nullptr) v = kmask[key] != 0;
+            vbits[g] = __ballot_sync(0xffffffffu, v);
+          }
+#pragma unroll
+          for (int i = 0; i < kBN; ++i) {
+            bool v = (vbits[i >> 5] >> (i & 31)) & 1u;
+            if (CAUSAL) v = v && (k0 + i <= q_row);
+            s[i] = v ? s[i] : -INFINITY;
+          }
+        }
+        float mx8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mx8[q] = s[q];
+#pragma unroll
+        for (int i = 8; i < kBN; i += 8)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mx8[q] = fmaxf(mx8[q], s[i + q]);
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        // Lazy rescaling: the exponent reference only moves when the tile max
+        // exceeds it by more than 8 (log2 units), so P <= 2^8 and O rescales
+        // are rare.  Exact in real arithmetic: the factor cancels in O / l.
+        const float m_tile = mx * p.scale_log2;
+        const float m_new = (m_tile > m_run + 8.f) ? m_tile : m_run;
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = fast_exp2(m_run - m_use);  // 1 unchanged, 0 from -inf
+        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float e0 = fast_exp2(fmaf(s[c * 32 + 2 * i], p.scale_log2, -m_use));
+            const float e1 = fast_exp2(fmaf(s[c * 32 + 2 * i + 1], p.scale_log2, -m_use));
+            sum8[(2 * i) & 7] += e0;
+            sum8[(2 * i + 1) & 7] += e1;
+            pk[i] = Pack<T>::two(e0, e1);
+          }
+          tmem_st16(t_s + c * 16, pk);  // P over the S columns already read
+        }
+        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+                          ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+        // Rescale O_t, which holds P(0..j-1) V (s_full implies the previous P.V
+        // completed); done after P so the S row is no longer live in registers.
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t o[32];
-            tmem_ld32(t_lane + kColO + c * 32, o);
+            tmem_ld32(t_o + c * 32, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_lane + kColO + c * 32, o);
+            tmem_st32(t_o + c * 32, o);
           }
         }
+        l_run = l_run * alpha + sum;
+        m_run = m_new;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[sb]);
-      m_run = m_new;
-    }
-    if (ok && mbar_wait_warp(o_done, (n_kv - 1) & 1, p.status, kDevTimeoutSoftmax, abort_flag)) {
+      if (!ok) break;
+      // epilogue: O_t / l -> ctx rows (heads merged)
+      if (!mbar_wait_warp(&o_final[t], of_phase, p.status, kDevTimeoutSoftmax, abort_flag)) break;
+      of_phase ^= 1u;
       tc_fence_after();
       const float inv_l = 1.f / l_run;
-      T* dst = static_cast<T*>(p.ctx) + ((int64_t)b * p.S + q_row) * p.D + h * HD;
+      T* dst = static_cast<T*>(p.ctx) + ((int64_t)it.b * p.S + q_row) * p.D + it.h * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
-        tmem_ld32(t_lane + kColO + c * 32, o);
+        tmem_ld32(t_o + c * 32, o);
         if (q_row < p.S) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
@@ -305,6 +398,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
           }
         }
       }
+      // The next item's first P.V overwrites O_t only after this thread's next
+      // p_full arrival, which follows these loads.
     }
   }
 
@@ -333,13 +428,16 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   p.S = (int)a.seq_len;
   p.H = (int)a.num_heads;
   p.D = (int)D;
-  p.num_q_tiles = (int)((a.seq_len + kBM - 1) / kBM);
+  p.num_pairs = (int)((a.seq_len + 2 * kBM - 1) / (2 * kBM));
+  const int64_t items = a.batch * a.num_heads * (int64_t)p.num_pairs;
+  if (items >= (int64_t)1 << 31) return fail(TTJ_ERR_UNSUPPORTED, "too many attention work items");
+  p.num_items = (int)items;
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
   p.status = a.status;
   auto kern = flash_fwd_kernel<T, HD, CAUSAL>;
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
-  dim3 grid((unsigned)(a.batch * a.num_heads), (unsigned)p.num_q_tiles);
-  kern<<<grid, 256, L::kTotal, stream>>>(tm, p);
+  const int grid = p.num_items < sm_count() ? p.num_items : sm_count();
+  kern<<<grid, kThreads, L::kTotal, stream>>>(tm, p);
   TTJ_CUDA_TRY(cudaGetLastError());
   return TTJ_OK;
 }

@@ -1,17 +1,28 @@
 // Persistent tcgen05 GEMM  y[M,N] = a[M,K] . b[N,K]^T  with fused epilogues.
 //
-// Roles (192 threads, one CTA per SM, persistent over output tiles):
+// Roles (320 threads per CTA, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A and B K-slices into a STAGES-deep shared ring
 //   warp 1      MMA issuer: one thread issues tcgen05.mma into a TMEM accumulator
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (one TMEM lane = one output
-//               row per thread), add bias / dequantise / add residual, store
+//   warps 2..9  epilogue: two warps per TMEM lane quarter (32 output rows), each
+//               taking half of the tile's columns in 64-column chunks
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Epilogue data path: for each 32-row x 64-column chunk a warp TMA-loads the
+// residual box (if any) into one of its two 4 KB staging buffers (128-byte
+// swizzle), tcgen05.ld's the 64 accumulator columns of its rows, adds bias /
+// dequantises / adds the residual in fp32, writes the 16-bit result back into
+// the same buffer and TMA-stores the box.  Full 128-byte lines move in both
+// directions; per-thread row-segment loads and stores (32 rows x 16 bytes per
+// warp instruction) were measured to cost more than the MMAs themselves.
 //
 // Operand tiles are 128-byte rows (64 fp16/bf16 or 128 int8 elements of K)
 // in TMA's 128-byte swizzle; each tcgen05.mma consumes 32 bytes of K.
 // Tiles are visited N-fastest so the CTAs resident at one time share a few
 // A row-blocks while the (smaller) weight matrix stays L2 resident.
+//
+// Two kernels share this epilogue: a single-CTA 128 x BN tile (for M <= 128)
+// and a CTA-pair (tcgen05 cta_group::2) 256 x BN tile for everything larger.
 #include <type_traits>
 
 #include "sm100_ptx.cuh"
@@ -22,64 +33,210 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kRowBytes = 128;  // bytes of K per smem row (one swizzle atom)
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiBoxRows = 32;
+constexpr int kEpiBoxCols = 64;                       // 16-bit: one 128-byte swizzle row
+constexpr int kEpiBoxBytes = kEpiBoxRows * 128;       // 4 KB
+constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBoxBytes;  // two buffers per warp: 64 KB
+constexpr int kBarrierBytes = 512;
 
 struct GemmParams {
   int M, N, K;
   int num_m_blocks, num_n_blocks;
   const void* bias;
-  const void* residual;
   const uint8_t* row_mask;
   const float* scale_a;
   const float* scale_b;
-  void* out;
+  void* out;  // only used by the int32 (raw accumulator) epilogue
   int* status;
 };
 
-template <typename TIn, int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int kABytes = kBM * kRowBytes;
-  static constexpr int kBBytes = BN * kRowBytes;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarrierBytes = 256;
-  static constexpr int kTotal = 1024 /*align slack*/ + STAGES * kStageBytes + kBarrierBytes;
+// Shared-memory layout common to both kernels: [stages][epilogue buffers][barriers].
+template <int STAGE_BYTES, int STAGES>
+struct GemmLayout {
+  static constexpr int kEpiOff = STAGES * STAGE_BYTES;
+  static constexpr int kBarOff = kEpiOff + kEpiBytes;
+  static constexpr int kTotal = 1024 /*align slack*/ + kBarOff + kBarrierBytes;
+  static_assert(kTotal <= 232448, "shared memory budget");
 };
 
-// Load 32 consecutive 16-bit values as floats (four 16-byte loads).
+// Per-warp epilogue state kept across tiles (scalars, so it stays in registers).
+struct EpiState {
+  uint8_t* buf0;       // two 1024-aligned 4 KB staging buffers
+  uint8_t* buf1;
+  uint64_t* bar0;      // residual-load barriers, one per buffer
+  uint64_t* bar1;
+  uint32_t phase0, phase1;
+  int next;            // buffer to use next
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk16) {
+  return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
 template <typename T>
-__device__ __forceinline__ void load32_f(const T* src, float (&v)[32]) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ void unpack8(uint4 w, float (&v)[8]) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w = __ldg(s + q);
-    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = Pack<T>::unpack(ws[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 w;
+  w.x = Pack<T>::two(v[0], v[1]);
+  w.y = Pack<T>::two(v[2], v[3]);
+  w.z = Pack<T>::two(v[4], v[5]);
+  w.w = Pack<T>::two(v[6], v[7]);
+  return w;
+}
+
+// Epilogue of one output tile for one warp.  t_row = TMEM address of this
+// thread's lane at the accumulator buffer's first column; row0 = first of the
+// warp's 32 output rows; the warp handles columns half `col_half` of
+// [n_blk*BN, n_blk*BN + BN).
+template <typename TOut, int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tm_out,
+                                              const CUtensorMap* tm_res, uint32_t t_row, int row0,
+                                              int n_blk, int col_half, EpiState& es,
+                                              int* status, volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  const int m = row0 + lane;
+  const bool row_ok = m < p.M;
+  if (row0 >= p.M) return;  // the warp's 32 rows are all past the last row (uniform)
+  if constexpr (EPI == (int)Epi::kRawS32) {
+    // Raw int32 accumulators (bit-exactness checks only): direct row stores.
+    constexpr int kChunks = BN / 32 / 2;
+#pragma unroll 1
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = col_half * kChunks + cc;
+      const int n0 = n_blk * BN + c * 32;
+      uint32_t r[32];
+      tmem_ld32(t_row + c * 32, r);
+      if (!row_ok || n0 >= p.N) continue;
+      int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(p.out) + (int64_t)m * p.N + n0);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = Pack<T>::unpack(ws[j]);
-      v[q * 8 + 2 * j] = f.x;
-      v[q * 8 + 2 * j + 1] = f.y;
+      for (int q = 0; q < 8; ++q)
+        dst[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]);
+    }
+    return;
+  } else {
+    constexpr bool kResidual = EPI == (int)Epi::kBiasResidual || EPI == (int)Epi::kDequantResidual;
+    constexpr bool kDequant = EPI == (int)Epi::kDequant || EPI == (int)Epi::kDequantResidual;
+    constexpr int kChunks = BN / kEpiBoxCols / 2;
+    float row_scale = 0.f;
+    bool row_keep = true;
+    if (kDequant && row_ok) row_scale = __ldg(p.scale_a + m);
+    if (row_ok && p.row_mask != nullptr) row_keep = __ldg(p.row_mask + m) != 0;
+#pragma unroll 1
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = col_half * kChunks + cc;
+      const int n0 = n_blk * BN + c * kEpiBoxCols;
+      const int b = es.next;
+      es.next ^= 1;
+      uint8_t* buf = b ? es.buf1 : es.buf0;
+      uint64_t* bar = b ? es.bar1 : es.bar0;
+      // The store issued from this buffer two chunks ago must have read it.
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      if (n0 >= p.N) continue;  // whole chunk past the last column (uniform)
+      if constexpr (kResidual) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar, kEpiBoxBytes);
+          tma_load_2d(buf, tm_res, bar, n0, row0);
+        }
+      }
+      uint32_t r[64];
+      tmem_ld64(t_row + c * kEpiBoxCols, r);  // warp-collective
+      if constexpr (kResidual) {
+        const uint32_t ph = b ? es.phase1 : es.phase0;
+        if (!mbar_wait_warp(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
+        if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = n0 + 8 * j;
+        float v[8];
+        if constexpr (!kDequant) {
+          float bias[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (col < p.N) unpack8<TOut>(__ldg(reinterpret_cast<const uint4*>(static_cast<const TOut*>(p.bias) + col)), bias);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * j + i]) + bias[i];
+        } else {
+          // k008 recipe order: acc * (s_a * s_w) + bias, each step rounded.
+          float ss[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          float bs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (col < p.N) {
+            const float4* sp = reinterpret_cast<const float4*>(p.scale_b + col);
+            const float4* bp = reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col);
+            const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1), b0 = __ldg(bp), b1 = __ldg(bp + 1);
+            ss[0] = s0.x; ss[1] = s0.y; ss[2] = s0.z; ss[3] = s0.w;
+            ss[4] = s1.x; ss[5] = s1.y; ss[6] = s1.z; ss[7] = s1.w;
+            bs[0] = b0.x; bs[1] = b0.y; bs[2] = b0.z; bs[3] = b0.w;
+            bs[4] = b1.x; bs[5] = b1.y; bs[6] = b1.z; bs[7] = b1.w;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float acc_f = static_cast<float>(static_cast<int32_t>(r[8 * j + i]));
+            v[i] = __fadd_rn(__fmul_rn(acc_f, __fmul_rn(row_scale, ss[i])), bs[i]);
+          }
+        }
+        uint4* slot = reinterpret_cast<uint4*>(buf + swz(lane, j));
+        if constexpr (kResidual) {
+          float res[8];
+          unpack8<TOut>(*slot, res);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = row_keep ? res[i] + v[i] : res[i];
+        } else {
+          // Output-row masking without a residual (the reference's masked_fill
+          // of the attention output, torch_transformer_benchmark.py:120-121).
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = row_keep ? v[i] : 0.f;
+        }
+        *slot = pack8<TOut>(v);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tm_out, buf, n0, row0);  // rows >= M / cols >= N are clipped
+        bulk_commit_group();
+      }
     }
   }
 }
 
-template <typename T>
-__device__ __forceinline__ void store32_f(T* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w;
-    w.x = Pack<T>::two(v[q * 8 + 0], v[q * 8 + 1]);
-    w.y = Pack<T>::two(v[q * 8 + 2], v[q * 8 + 3]);
-    w.z = Pack<T>::two(v[q * 8 + 4], v[q * 8 + 5]);
-    w.w = Pack<T>::two(v[q * 8 + 6], v[q * 8 + 7]);
-    d[q] = w;
-  }
+template <typename TIn>
+constexpr CUtensorMapDataType tmap_dtype() {
+  return std::is_same<TIn, int8_t>::value    ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+         : std::is_same<TIn, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
 
+template <typename TOut>
+__device__ __forceinline__ void init_epi_state(EpiState& es, uint8_t* epi_base, uint64_t* res_bars, int ew) {
+  es.buf0 = epi_base + (2 * ew) * kEpiBoxBytes;
+  es.buf1 = epi_base + (2 * ew + 1) * kEpiBoxBytes;
+  es.bar0 = res_bars + 2 * ew;
+  es.bar1 = res_bars + 2 * ew + 1;
+  es.phase0 = es.phase1 = 0u;
+  es.next = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Single-CTA kernel: one 128 x BN tile per CTA.
 template <typename TIn, typename TOut, int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                const GemmParams p) {
-  using L = GemmSmem<TIn, BN, STAGES>;
+  constexpr int kABytes = kBM * kRowBytes;
+  constexpr int kBBytes = BN * kRowBytes;
+  using L = GemmLayout<kABytes + kBBytes, STAGES>;
   constexpr bool kInt8 = std::is_same<TIn, int8_t>::value;
   constexpr int kBK = kRowBytes / sizeof(TIn);             // K elements per stage
   constexpr uint32_t kTmemCols = 2 * BN;                   // 256 or 512
@@ -92,13 +249,15 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * L::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint8_t* epi_base = smem + L::kEpiOff;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* res_bars = drain + 1;  // [2 * kEpiWarps]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bars + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -111,9 +270,10 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&res_bars[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -146,9 +306,9 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(sA + stage * L::kABytes, &tmA, &full[stage], kb * kBK, m_blk * kBM);
-          tma_load_2d(sB + stage * L::kBBytes, &tmB, &full[stage], kb * kBK, n_blk * BN);
+          mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes);
+          tma_load_2d(sA + stage * kABytes, &tmA, &full[stage], kb * kBK, m_blk * kBM);
+          tma_load_2d(sB + stage * kBBytes, &tmB, &full[stage], kb * kBK, n_blk * BN);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -178,8 +338,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * L::kABytes);
-          const uint32_t b_addr = smem_u32(sB + stage * L::kBBytes);
+          const uint32_t a_addr = smem_u32(sA + stage * kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
 #pragma unroll
           for (int kk = 0; kk < kRowBytes / 32; ++kk) {
             const uint64_t ad = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
@@ -205,8 +365,10 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int lane_grp = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = lane_grp * 32 + lane;
+    const int lane_grp = warp & 3;            // TMEM lane quarter this warp may access
+    const int col_half = (warp - 2) >> 2;     // which half of the tile's columns
+    EpiState es;
+    init_epi_state<TOut>(es, epi_base, res_bars, warp - 2);
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -215,69 +377,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc_fence_after();
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;
-      const int m = m_blk * kBM + row;
-      const bool row_ok = m < p.M;
-      float row_scale = 0.f;
-      bool row_keep = true;
-      if constexpr (EPI == (int)Epi::kDequant || EPI == (int)Epi::kDequantResidual) {
-        if (row_ok) row_scale = __ldg(p.scale_a + m);
-      }
-      if constexpr (EPI != (int)Epi::kRawS32) {
-        if (row_ok && p.row_mask != nullptr) row_keep = __ldg(p.row_mask + m) != 0;
-      }
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);  // warp-collective: every lane executes it
-        const int n0 = n_blk * BN + c * 32;
-        if (!row_ok || n0 >= p.N) continue;
-        if constexpr (EPI == (int)Epi::kRawS32) {
-          int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(p.out) + (int64_t)m * p.N + n0);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            dst[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]);
-        } else {
-          float v[32];
-          if constexpr (EPI == (int)Epi::kBias || EPI == (int)Epi::kBiasResidual) {
-            float b[32];
-            load32_f(static_cast<const TOut*>(p.bias) + n0, b);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + b[i];
-          } else {
-            // k008 recipe order: acc * (s_a * s_w) + bias, each step rounded.
-            const float4* sb = reinterpret_cast<const float4*>(p.scale_b + n0);
-            const float4* bb = reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + n0);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 s4 = __ldg(sb + q);
-              const float4 b4 = __ldg(bb + q);
-              const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
-              const float bs[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float acc_f = static_cast<float>(static_cast<int32_t>(r[4 * q + j]));
-                v[4 * q + j] = __fadd_rn(__fmul_rn(acc_f, __fmul_rn(row_scale, ss[j])), bs[j]);
-              }
-            }
-          }
-          if constexpr (EPI == (int)Epi::kBiasResidual || EPI == (int)Epi::kDequantResidual) {
-            float res[32];
-            load32_f(static_cast<const TOut*>(p.residual) + (int64_t)m * p.N + n0, res);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = row_keep ? res[i] + v[i] : res[i];
-          } else {
-            // Output-row masking without a residual (reference masked_fill of the
-            // attention output, torch_transformer_benchmark.py:120-121).
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = row_keep ? v[i] : 0.f;
-          }
-          store32_f(static_cast<TOut*>(p.out) + (int64_t)m * p.N + n0, v);
-        }
-      }
+      epilogue_tile<TOut, BN, EPI>(p, &tmOut, &tmRes,
+                                   tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * BN,
+                                   m_blk * kBM + lane_grp * 32, n_blk, col_half, es, p.status, abort_flag);
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    if (lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -286,57 +393,289 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 0) tmem_dealloc(tmem_base, kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair kernel (cluster of 2, tcgen05 cta_group::2): one 256 x BN output
+// tile per pair.  Each CTA loads its own 128 rows of A and its half (BN/2 rows)
+// of B, so per SM the operand traffic per FLOP is 2/3 of the single-CTA
+// 128 x BN tile.  The leader CTA (rank 0) issues every MMA; D rows 0..127 land
+// in the leader's TMEM, rows 128..255 in the peer's.  Both CTAs' TMA loads count
+// their bytes on the leader's full barrier; the leader commits stage-free and
+// accumulator-full events to both CTAs' barriers (two plain commits, no
+// multicast); both CTAs' epilogue warps release an accumulator by arriving on
+// the leader's barrier.
 template <typename TIn, typename TOut, int BN, int STAGES, int EPI>
-int launch_one(const GemmArgs& g, cudaStream_t stream) {
-  using L = GemmSmem<TIn, BN, STAGES>;
+__global__ void __launch_bounds__(kGemmThreads, 1) __cluster_dims__(2, 1, 1)
+gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
+                    const GemmParams p) {
+  constexpr int kABytes = kBM * kRowBytes;         // this CTA's 128 rows of A
+  constexpr int kBBytes = (BN / 2) * kRowBytes;    // this CTA's half of B
+  constexpr int kStageBytes = kABytes + kBBytes;
+  using L = GemmLayout<kStageBytes, STAGES>;
+  constexpr bool kInt8 = std::is_same<TIn, int8_t>::value;
   constexpr int kBK = kRowBytes / sizeof(TIn);
-  const CUtensorMapDataType dt = std::is_same<TIn, int8_t>::value ? CU_TENSOR_MAP_DATA_TYPE_UINT8
-                                 : std::is_same<TIn, __half>::value
-                                     ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap ta, tb;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc =
+      kInt8 ? idesc_i8(2 * kBM, BN)
+            : idesc_f16(2 * kBM, BN, std::is_same<TIn, __nv_bfloat16>::value ? 1 : 0, 0);
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of 2");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint8_t* epi_base = smem + L::kEpiOff;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint64_t* res_bars = drain + 1;  // [2 * kEpiWarps]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bars + 2 * kEpiWarps);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);    // the leader's copy counts both CTAs' bytes
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);  // leader's copy: every epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&res_bars[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;   // m blocks of 256 rows
+  const int num_kb = (p.K + kBK - 1) / kBK;
+  const int pair_id = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+        const int m_blk = tile / p.num_n_blocks;
+        const int n_blk = tile - m_blk * p.num_n_blocks;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+          tma_load_2d_pair(sA + stage * kABytes, &tmA, leader_full, kb * kBK,
+                           m_blk * 2 * kBM + (int)rank * kBM);
+          tma_load_2d_pair(sB + stage * kBBytes, &tmB, leader_full, kb * kBK,
+                           n_blk * BN + (int)rank * (BN / 2));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair_id; ok && tile < num_tiles; tile += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutAccEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kDevTimeoutTmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kRowBytes / 32; ++kk) {
+            const uint64_t ad = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+            if constexpr (kInt8)
+              umma_i8_ss_pair(d_tmem, ad, bd, kIdesc, accum);
+            else
+              umma_f16_ss_pair(d_tmem, ad, bd, kIdesc, accum);
+          }
+          const uint32_t e = smem_u32(&empty[stage]);
+          umma_commit_pair(mapa_shared(e, 0));  // stage free in both CTAs once read
+          umma_commit_pair(mapa_shared(e, 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&acc_full[acc]);
+        umma_commit_pair(mapa_shared(f, 0));
+        umma_commit_pair(mapa_shared(f, 1));
+      }
+      umma_commit_pair(mapa_shared(smem_u32(drain), 0));
+      mbar_wait(drain, 0, p.status, kDevTimeoutAccFull, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int lane_grp = warp & 3;
+    const int col_half = (warp - 2) >> 2;
+    EpiState es;
+    init_epi_state<TOut>(es, epi_base, res_bars, warp - 2);
+    int local = 0;
+    for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, p.status, kDevTimeoutAccFull, abort_flag)) break;
+      tc_fence_after();
+      const int m_blk = tile / p.num_n_blocks;
+      const int n_blk = tile - m_blk * p.num_n_blocks;
+      epilogue_tile<TOut, BN, EPI>(p, &tmOut, &tmRes,
+                                   tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * BN,
+                                   m_blk * 2 * kBM + (int)rank * kBM + lane_grp * 32, n_blk, col_half, es,
+                                   p.status, abort_flag);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+    }
+    if (lane == 0) bulk_wait_group_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into the peer's TMEM / smem are complete
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc_pair(tmem_base, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+template <typename TIn, typename TOut, int EPI>
+int make_maps(const GemmArgs& g, int box_a_rows, int box_b_rows, CUtensorMap* ta, CUtensorMap* tb,
+              CUtensorMap* tout, CUtensorMap* tres) {
+  constexpr int kBK = kRowBytes / sizeof(TIn);
+  const CUtensorMapDataType dt = tmap_dtype<TIn>();
   {
     const uint64_t dims[2] = {(uint64_t)g.k, (uint64_t)g.m};
     const uint64_t strides[1] = {(uint64_t)g.k * sizeof(TIn)};
-    const uint32_t box[2] = {(uint32_t)kBK, (uint32_t)kBM};
-    int rc = encode_tmap(&ta, dt, 2, g.a, dims, strides, box);
-    if (rc) return rc;
+    const uint32_t box[2] = {(uint32_t)kBK, (uint32_t)box_a_rows};
+    if (int rc = encode_tmap(ta, dt, 2, g.a, dims, strides, box)) return rc;
   }
   {
     const uint64_t dims[2] = {(uint64_t)g.k, (uint64_t)g.n};
     const uint64_t strides[1] = {(uint64_t)g.k * sizeof(TIn)};
-    const uint32_t box[2] = {(uint32_t)kBK, (uint32_t)BN};
-    int rc = encode_tmap(&tb, dt, 2, g.b, dims, strides, box);
-    if (rc) return rc;
+    const uint32_t box[2] = {(uint32_t)kBK, (uint32_t)box_b_rows};
+    if (int rc = encode_tmap(tb, dt, 2, g.b, dims, strides, box)) return rc;
   }
+  if constexpr (EPI == (int)Epi::kRawS32) {
+    *tout = *ta;  // unused by the raw epilogue
+    *tres = *ta;
+  } else {
+    const CUtensorMapDataType odt = tmap_dtype<TOut>();
+    const uint64_t dims[2] = {(uint64_t)g.n, (uint64_t)g.m};
+    const uint64_t strides[1] = {(uint64_t)g.n * sizeof(TOut)};
+    const uint32_t box[2] = {(uint32_t)kEpiBoxCols, (uint32_t)kEpiBoxRows};
+    if (int rc = encode_tmap(tout, odt, 2, g.out, dims, strides, box)) return rc;
+    if (g.residual != nullptr) {
+      if (int rc = encode_tmap(tres, odt, 2, g.residual, dims, strides, box)) return rc;
+    } else {
+      *tres = *tout;  // unused
+    }
+  }
+  return TTJ_OK;
+}
+
+GemmParams make_params(const GemmArgs& g, int tile_m, int bn) {
   GemmParams p;
   p.M = (int)g.m;
   p.N = (int)g.n;
   p.K = (int)g.k;
-  p.num_m_blocks = (int)((g.m + kBM - 1) / kBM);
-  p.num_n_blocks = (int)((g.n + BN - 1) / BN);
+  p.num_m_blocks = (int)((g.m + tile_m - 1) / tile_m);
+  p.num_n_blocks = (int)((g.n + bn - 1) / bn);
   p.bias = g.bias;
-  p.residual = g.residual;
   p.row_mask = g.row_mask;
   p.scale_a = g.scale_a;
   p.scale_b = g.scale_b;
   p.out = g.out;
   p.status = g.status;
+  return p;
+}
+
+template <typename TIn, typename TOut, int BN, int STAGES, int EPI>
+int launch_one(const GemmArgs& g, cudaStream_t stream) {
+  using L = GemmLayout<kBM * kRowBytes + BN * kRowBytes, STAGES>;
+  CUtensorMap ta, tb, tout, tres;
+  if (int rc = make_maps<TIn, TOut, EPI>(g, kBM, BN, &ta, &tb, &tout, &tres)) return rc;
+  const GemmParams p = make_params(g, kBM, BN);
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   auto kern = gemm_tn_kernel<TIn, TOut, BN, STAGES, EPI>;
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
-  kern<<<grid, 192, L::kTotal, stream>>>(ta, tb, p);
+  kern<<<grid, kGemmThreads, L::kTotal, stream>>>(ta, tb, tout, tres, p);
+  TTJ_CUDA_TRY(cudaGetLastError());
+  return TTJ_OK;
+}
+
+template <typename TIn, typename TOut, int BN, int STAGES, int EPI>
+int launch_pair(const GemmArgs& g, cudaStream_t stream) {
+  using L = GemmLayout<kBM * kRowBytes + (BN / 2) * kRowBytes, STAGES>;
+  CUtensorMap ta, tb, tout, tres;
+  if (int rc = make_maps<TIn, TOut, EPI>(g, kBM, BN / 2, &ta, &tb, &tout, &tres)) return rc;
+  const GemmParams p = make_params(g, 2 * kBM, BN);
+  const int tiles = p.num_m_blocks * p.num_n_blocks;
+  const int max_pairs = sm_count() / 2;
+  const int grid = 2 * (tiles < max_pairs ? tiles : max_pairs);
+  auto kern = gemm_tn_pair_kernel<TIn, TOut, BN, STAGES, EPI>;
+  TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+  kern<<<grid, kGemmThreads, L::kTotal, stream>>>(ta, tb, tout, tres, p);
   TTJ_CUDA_TRY(cudaGetLastError());
   return TTJ_OK;
 }
 
 template <typename TIn, typename TOut, int EPI>
 int dispatch_bn(const GemmArgs& g, cudaStream_t stream) {
-  // BN = 256 halves the A re-reads; BN = 128 when N is small or would waste a
-  // half-empty tile column.
-  if (g.n % 256 == 0 && g.n >= 512) return launch_one<TIn, TOut, 256, 4, EPI>(g, stream);
-  return launch_one<TIn, TOut, 128, 6, EPI>(g, stream);
+  // More than one 128-row block: CTA pairs with 256 x 256 (or 256 x 128) tiles.
+  // Otherwise one CTA per 128 x BN tile.  BN = 256 halves the A re-reads; 128
+  // when N is small or would leave a half-empty tile column.
+  const bool wide = g.n % 256 == 0 && g.n >= 512;
+  if (g.m > kBM) {
+    if (wide) return launch_pair<TIn, TOut, 256, 4, EPI>(g, stream);
+    return launch_pair<TIn, TOut, 128, 5, EPI>(g, stream);
+  }
+  if (wide) return launch_one<TIn, TOut, 256, 3, EPI>(g, stream);
+  return launch_one<TIn, TOut, 128, 4, EPI>(g, stream);
 }
 
 template <typename TIn, typename TOut>
