@@ -16,20 +16,24 @@
 //   warp 2       TMA: the two Q tiles of each work item
 //   warps 3..6   softmax for tile A, warps 7..10 for tile B: thread = query row;
 //                load the S row from TMEM, mask, online softmax in fp32 with a
-//                lazily moved row max, write P (input dtype) back over S, rescale
-//                its O row when the max moved, and at the end normalise O and
-//                store the context row at the head's columns of ctx[B,S,D].
-// The two softmax warpgroups run on different tiles, so the tensor core works on
-// one tile while the other tile's exponentials are computed.
+//                lazily moved row max, write P (input dtype) to TMEM, rescale its
+//                O row when the max moved, and at the end normalise O and store
+//                the context row at the head's columns of ctx[B,S,D] (head merge).
 //
-// MMA issue order per tile t and key tile j:  PV_t(j-1), QK_t(j), commit s_full_t.
-// tcgen05.commit arrives only when EVERY earlier MMA of the issuing thread has
-// completed, so "S_t(j) is ready" also means "P_t(j-1) has been consumed and O_t
-// holds P_t(0..j-1) V": the softmax may then overwrite S_t with P_t(j) and rescale
-// O_t without further barriers.
+// Two schedules, chosen by what fits in the 512 TMEM columns:
 //
-// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,256+HD) O_B [256+HD,256+2HD);
-// P_t (16-bit, two per column) overwrites the first 64 columns of S_t.
+// head_dim 64 ("separate P"): S_A [0,128) S_B [128,256) P_A [256,320)
+//   P_B [320,384) O_A [384,448) O_B [448,512).  S_t(j+1) = Q_t K_{j+1}^T is
+//   issued as soon as the softmax has read S_t(j) out of TMEM, so it is ready
+//   when the softmax finishes tile j; P_t(j) goes to its own buffer once
+//   P_t(j-1) V_{j-1} has completed (o_done).  The softmax never waits for the
+//   tensor core in steady state (measured: with P written over S the softmax
+//   idled ~40% of each step waiting for the P.V -> Q.K round trip).
+// head_dim 128 ("P over S"): S_A [0,128) S_B [128,256) O_A [256,384)
+//   O_B [384,512); P_t overwrites the first 64 columns of S_t, so the issue
+//   order per tile is PV_t(j-1), QK_t(j), commit s_full_t.  tcgen05.commit
+//   arrives only when every earlier MMA of the issuing thread has completed,
+//   so "S_t(j) is ready" also means P_t(j-1) was consumed and O_t is stable.
 #include "sm100_ptx.cuh"
 #include "ttj_internal.h"
 
@@ -54,6 +58,7 @@ struct AttnParams {
 
 template <int HD>
 struct AttnSmem {
+  static constexpr bool kSepP = HD == 64;           // separate P buffers in TMEM
   static constexpr int kStages = HD == 64 ? 4 : 2;
   static constexpr int kTileBytes = HD * 2 * 128;  // 128 rows x HD x 2 bytes
   static constexpr int kQOff = 0;                   // Q_A, Q_B
@@ -61,12 +66,53 @@ struct AttnSmem {
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kTotal = 1024 + kBarOff + 512;
+  // TMEM columns
+  static constexpr uint32_t kColP = kSepP ? 256 : 0;      // + t*64 (separate) / + t*128 (over S)
+  static constexpr uint32_t kColO = kSepP ? 384 : 256;    // + t*HD
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Two fp16 exponentials in one MUFU operation, result already packed for P.
+__device__ __forceinline__ uint32_t exp2_h2(uint32_t x2) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x2));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// sm_100 packed fp32 pairs (two lanes per instruction) and 3-input max.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Decode work item -> (b, h, pair).  Causal items are ordered by decreasing
@@ -98,11 +144,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   using L = AttnSmem<HD>;
   constexpr int ST = L::kStages;
+  constexpr bool kSepP = L::kSepP;
   constexpr int kChunks = HD / 64;
   constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdescQK = idesc_f16(kBM, kBN, kBf16, 0);
   constexpr uint32_t kIdescPV = idesc_f16(kBM, HD, kBf16, 1);
-  constexpr uint32_t kColO = 256;
+  constexpr uint32_t kPStride = kSepP ? 64 : 128;  // P column stride between tiles
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -117,10 +164,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   uint64_t* k_empty = k_full + ST;      // [ST]
   uint64_t* v_full = k_empty + ST;      // [ST]
   uint64_t* v_empty = v_full + ST;      // [ST]
-  uint64_t* s_full = v_empty + ST;      // [2] per tile
-  uint64_t* p_full = s_full + 2;        // [2] per tile
-  uint64_t* o_final = p_full + 2;       // [2] per tile
-  uint64_t* drain = o_final + 2;        // [1]
+  uint64_t* s_full = v_empty + ST;      // [2] per tile: S_t written
+  uint64_t* s_free = s_full + 2;        // [2] per tile: S_t read by the softmax (separate P)
+  uint64_t* p_full = s_free + 2;        // [2] per tile: P_t written
+  uint64_t* o_done = p_full + 2;        // [2] per tile: one phase per completed P_t V
+  uint64_t* drain = o_done + 2;         // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -138,8 +186,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 128);
       mbar_init(&p_full[t], 128);
-      mbar_init(&o_final[t], 1);
+      mbar_init(&o_done[t], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -198,6 +247,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     if (lane == 0) {
       int kv = 0, k = 0;
       uint32_t pf_phase[2] = {0u, 0u};
+      uint32_t sfree_phase[2] = {0u, 0u};
+      int qk_count[2] = {0, 0};
       bool ok = true;
       auto qk = [&](int t, int st) {
         const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
@@ -214,10 +265,23 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           // V is MN-major: 16 keys = 16 rows of 128 bytes; next 64-column chunk at +16 KB.
-          umma_f16_ts(tmem + kColO + t * HD, tmem + t * 128 + kk * 8,
+          umma_f16_ts(tmem + L::kColO + t * HD, tmem + L::kColP + t * kPStride + kk * 8,
                       smem_desc_sw128(v_addr + kk * 16 * 128, kChunkBytes, 1024), kIdescPV,
                       (accumulate || kk > 0) ? 1u : 0u);
         }
+      };
+      // Separate-P schedule: QK_t may overwrite S_t once the softmax has read the
+      // previous S_t (s_free), including the last one of the previous item.
+      auto issue_qk_sep = [&](int t, int st) -> bool {
+        if (qk_count[t] > 0) {
+          if (!mbar_wait(&s_free[t], sfree_phase[t], p.status, kDevTimeoutSoftmax, abort_flag)) return false;
+          sfree_phase[t] ^= 1u;
+        }
+        tc_fence_after();
+        qk(t, st);
+        umma_commit(&s_full[t]);
+        ++qk_count[t];
+        return true;
       };
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++k) {
         const Item it = decode_item<CAUSAL>(item, p);
@@ -229,12 +293,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
         {
           const int st = kv0 % ST;
           if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-          tc_fence_after();
-          qk(0, st);
-          umma_commit(&s_full[0]);
-          qk(1, st);
-          umma_commit(&s_full[1]);
+          if constexpr (kSepP) {
+            if (!issue_qk_sep(0, st) || !issue_qk_sep(1, st)) break;
+          } else {
+            tc_fence_after();
+            qk(0, st);
+            umma_commit(&s_full[0]);
+            qk(1, st);
+            umma_commit(&s_full[1]);
+          }
           umma_commit(&k_empty[st]);
+          if (n_b == 1) umma_commit(q_empty);
         }
         for (int j = 0; j < n_b; ++j) {
           const int st = (kv0 + j) % ST;
@@ -242,35 +311,59 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
           const int st_n = (kv0 + j + 1) % ST;
           const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
           const bool next_b = j + 1 < n_b;
-          if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
           if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-          if (j < n_a) {
-            if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-            pf_phase[0] ^= 1u;
-            tc_fence_after();
-            pv(0, st, j > 0);
-            if (j + 1 < n_a) {
-              qk(0, st_n);
-              umma_commit(&s_full[0]);
-            } else {
-              umma_commit(&o_final[0]);
+          if constexpr (kSepP) {
+            // next scores first, then this step's P.V products
+            if (next_b) {
+              if (j + 1 < n_a && !issue_qk_sep(0, st_n)) { ok = false; break; }
+              if (!issue_qk_sep(1, st_n)) { ok = false; break; }
+              umma_commit(&k_empty[st_n]);
+              if (j + 2 == n_b) umma_commit(q_empty);  // last QK of the item issued
             }
-          }
-          if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-          pf_phase[1] ^= 1u;
-          tc_fence_after();
-          pv(1, st, j > 0);
-          umma_commit(&v_empty[st]);
-          if (next_b) {
-            qk(1, st_n);
-            umma_commit(&s_full[1]);
-            umma_commit(&k_empty[st_n]);
+            if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+            if (j < n_a) {
+              if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+              pf_phase[0] ^= 1u;
+              tc_fence_after();
+              pv(0, st, j > 0);
+              umma_commit(&o_done[0]);
+            }
+            if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            pf_phase[1] ^= 1u;
+            tc_fence_after();
+            pv(1, st, j > 0);
+            umma_commit(&o_done[1]);
+            umma_commit(&v_empty[st]);
           } else {
-            umma_commit(&o_final[1]);
+            if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+            if (j < n_a) {
+              if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+              pf_phase[0] ^= 1u;
+              tc_fence_after();
+              pv(0, st, j > 0);
+              if (j + 1 < n_a) {
+                qk(0, st_n);
+                umma_commit(&s_full[0]);
+              } else {
+                umma_commit(&o_done[0]);
+              }
+            }
+            if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            pf_phase[1] ^= 1u;
+            tc_fence_after();
+            pv(1, st, j > 0);
+            umma_commit(&v_empty[st]);
+            if (next_b) {
+              qk(1, st_n);
+              umma_commit(&s_full[1]);
+              umma_commit(&k_empty[st_n]);
+              if (j + 2 == n_b) umma_commit(q_empty);
+            } else {
+              umma_commit(&o_done[1]);
+            }
           }
         }
         kv = kv0 + n_b;
-        umma_commit(q_empty);  // every QK of this item has completed
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.status, kDevTimeoutSoftmax, nullptr);
@@ -282,8 +375,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     const int r = lg * 32 + lane;        // query row within the tile
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(lg * 32) << 16);
     const uint32_t t_s = t_lane + t * 128;
-    const uint32_t t_o = t_lane + kColO + t * HD;
-    uint32_t sf_phase = 0, of_phase = 0;
+    const uint32_t t_p = t_lane + L::kColP + t * kPStride;
+    const uint32_t t_o = t_lane + L::kColO + t * HD;
+    uint32_t sf_phase = 0;
+    uint32_t od_phase = 0;  // o_done parity of the next P.V to wait for
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
       const Item it = decode_item<CAUSAL>(item, p);
@@ -303,6 +398,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
           tmem_ld128(t_s, u);
 #pragma unroll
           for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(u[i]);
+        }
+        if constexpr (kSepP) {
+          tc_fence_before();
+          mbar_arrive(&s_free[t]);  // the tensor core may overwrite S_t now
         }
         const int k0 = j * kBN;
         const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && k0 + kBN - 1 > q0) || kmask != nullptr;
@@ -324,15 +423,18 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
             s[i] = v ? s[i] : -INFINITY;
           }
         }
+        // Row max: eight independent chains of 3-input max.
         float mx8[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) mx8[q] = s[q];
+        for (int q = 0; q < 8; ++q) mx8[q] = fmax3(s[q], s[8 + q], s[16 + q]);
 #pragma unroll
-        for (int i = 8; i < kBN; i += 8)
+        for (int i = 24; i < kBN - 8; i += 16)
 #pragma unroll
-          for (int q = 0; q < 8; ++q) mx8[q] = fmaxf(mx8[q], s[i + q]);
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+          for (int q = 0; q < 8; ++q) mx8[q] = fmax3(mx8[q], s[i + q], s[i + 8 + q]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mx8[q] = fmaxf(mx8[q], s[kBN - 8 + q]);
+        const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7]));
         // Lazy rescaling: the exponent reference only moves when the tile max
         // exceeds it by more than 8 (log2 units), so P <= 2^8 and O rescales
         // are rare.  Exact in real arithmetic: the factor cancels in O / l.
@@ -340,24 +442,69 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
         const float m_new = (m_tile > m_run + 8.f) ? m_tile : m_run;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
         const float alpha = fast_exp2(m_run - m_use);  // 1 unchanged, 0 from -inf
-        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float e0 = fast_exp2(fmaf(s[c * 32 + 2 * i], p.scale_log2, -m_use));
-            const float e1 = fast_exp2(fmaf(s[c * 32 + 2 * i + 1], p.scale_log2, -m_use));
-            sum8[(2 * i) & 7] += e0;
-            sum8[(2 * i + 1) & 7] += e1;
-            pk[i] = Pack<T>::two(e0, e1);
-          }
-          tmem_st16(t_s + c * 16, pk);  // P over the S columns already read
+        if (kSepP && j > 0) {
+          // P_t(j-1) V must have completed: it read the P buffer written below
+          // and it is the last write to O_t before a rescale.  It was issued
+          // about one softmax step ago, so this wait is normally free.
+          if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+          od_phase ^= 1u;
+          tc_fence_after();
         }
-        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
-                          ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-        // Rescale O_t, which holds P(0..j-1) V (s_full implies the previous P.V
-        // completed); done after P so the S row is no longer live in registers.
+        // x = s * scale_log2 - m as packed pairs; P = 2^x, written to TMEM 16
+        // columns (32 keys) at a time: its own buffer, or over the S columns
+        // already read.
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t nm2 = f2_pack(-m_use, -m_use);
+        float sum;
+        if constexpr (!kBf16) {
+          // fp16: x <= 8, so 2^x <= 256 fits fp16; exponentials two per MUFU op,
+          // row sums accumulated as fp16 pairs in 16 short chains (<= 4 adds
+          // each), finished in fp32.
+          uint32_t hs[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int ii = 0; ii < 16; ++ii) {
+              const int i = c * 16 + ii;
+              float x0, x1;
+              f2_unpack(ffma2(f2_pack(s[2 * i], s[2 * i + 1]), c2, nm2), x0, x1);
+              pk[ii] = exp2_h2(Pack<__half>::two(x0, x1));
+              hs[i & 7] = (i < 8) ? pk[ii] : hadd2_u(hs[i & 7], pk[ii]);
+            }
+            tmem_st16(t_p + c * 16, pk);
+          }
+          float acc = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float2 f = Pack<__half>::unpack(hs[q]);
+            acc += f.x + f.y;
+          }
+          sum = acc;
+        } else {
+          uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int ii = 0; ii < 16; ++ii) {
+              const int i = c * 16 + ii;
+              float x0, x1;
+              f2_unpack(ffma2(f2_pack(s[2 * i], s[2 * i + 1]), c2, nm2), x0, x1);
+              const float e0 = fast_exp2(x0);
+              const float e1 = fast_exp2(x1);
+              pk[ii] = Pack<T>::two(e0, e1);
+              sum2[i & 3] = fadd2(sum2[i & 3], f2_pack(e0, e1));
+            }
+            tmem_st16(t_p + c * 16, pk);
+          }
+          float a0, a1;
+          f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), a0, a1);
+          sum = a0 + a1;
+        }
+        l_run = l_run * alpha + sum;
+        m_run = m_new;
+        // Rescale O_t when the exponent reference moved (O_t holds P(0..j-1) V).
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
@@ -368,16 +515,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
             tmem_st32(t_o + c * 32, o);
           }
         }
-        l_run = l_run * alpha + sum;
-        m_run = m_new;
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      // epilogue: O_t / l -> ctx rows (heads merged)
-      if (!mbar_wait_warp(&o_final[t], of_phase, p.status, kDevTimeoutSoftmax, abort_flag)) break;
-      of_phase ^= 1u;
+      // epilogue: wait for the last P.V, then O_t / l -> ctx rows (heads merged)
+      if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) break;
+      od_phase ^= 1u;
       tc_fence_after();
       const float inv_l = 1.f / l_run;
       T* dst = static_cast<T*>(p.ctx) + ((int64_t)it.b * p.S + q_row) * p.D + it.h * HD;
