@@ -92,6 +92,20 @@ int ttj_linear_fwd(const void* x, const void* w, const void* bias, const void* r
                    int dtype, int* status, ttj_stream_t stream);
 
 /*
+ * ttj_linear_fwd with the input stored K-chunk-major:
+ *   x(m, k) = x_chunks[k / k_chunk][m][k % k_chunk],  x_chunks [k/k_chunk][m][k_chunk]
+ * This is the layout a head-sharded attention context arrives in when each of
+ * k/k_chunk ranks contributes the columns of its heads ([m][k_chunk] each): the
+ * out-projection reads it in place (a 3-D tensor map), so the gathered slices
+ * need no re-packing into [m][k].  Requires k_chunk % 64 == 0, k % k_chunk == 0,
+ * n % 32 == 0.  Used by the multi-GPU head partitioner; the reference has no
+ * multi-GPU path (its out_proj is torch_transformer_benchmark.py:118).
+ */
+int ttj_linear_kchunked_fwd(const void* x_chunks, int64_t k_chunk, const void* w, const void* bias,
+                            const void* residual, const uint8_t* row_mask, void* y, int64_t m,
+                            int64_t n, int64_t k, int dtype, int* status, ttj_stream_t stream);
+
+/*
  * Fused QKV projection: qkv[T,3D] = x[T,D] . w_qkv[3D,D]^T + b_qkv.
  * Replaces q_proj/k_proj/v_proj + _split_heads (torch_transformer_benchmark.py:77-83,
  * :93-95): the head split is free because attention reads head slices of the

@@ -112,3 +112,18 @@ def test_weight_quantizer_matches_recipe():
     q, s = ops.quantize_weight(w.cuda())
     q_ref, s_ref = quant_weight_ref(w)
     assert torch.equal(q.cpu(), q_ref) and torch.equal(s.cpu(), s_ref)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("m,n,k,kc", [(512, 1024, 1024, 128), (777, 512, 512, 64), (4096, 4096, 4096, 512)])
+def test_linear_kchunked_matches_plain(dt, m, n, k, kc):
+    """Input stored K-chunk-major [k/kc, m, kc] (the head-sharded gather layout)."""
+    g = torch.Generator().manual_seed(m + kc)
+    x, w = _rand((m, k), g, 1.0, DT[dt]), _rand((n, k), g, k ** -0.5, DT[dt])
+    b, res = _rand((n,), g, 0.1, DT[dt]), _rand((m, n), g, 1.0, DT[dt])
+    chunks = x.view(m, k // kc, kc).permute(1, 0, 2).contiguous()
+    y = ops.linear_kchunked(chunks, w, b, residual=res)
+    y_plain = ops.linear(x, w, b, residual=res)
+    assert torch.equal(y, y_plain)  # same tiles, same order of accumulation
+    rep = compare_outputs(res.float() + x.float() @ w.float().T + b.float(), y.float())
+    assert rep.passed, str(rep)

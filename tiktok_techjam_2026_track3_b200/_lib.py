@@ -26,7 +26,7 @@ STATUS_NAMES = {
 EXPORTED_SYMBOLS = (
     "ttj_version", "ttj_status_string", "ttj_last_error", "ttj_read_status",
     "ttj_selftest_wait_timeout",
-    "ttj_linear_fwd", "ttj_qkv_proj_fwd", "ttj_flash_attn_fwd", "ttj_out_proj_residual_fwd",
+    "ttj_linear_fwd", "ttj_linear_kchunked_fwd", "ttj_qkv_proj_fwd", "ttj_flash_attn_fwd", "ttj_out_proj_residual_fwd",
     "ttj_attn_layer_workspace_size", "ttj_attn_layer_fwd", "ttj_attn_layer_fwd_noalloc",
     "ttj_int8_quant_rows", "ttj_int8_gemm_s32", "ttj_int8_linear_fwd",
     "ttj_int8_attn_layer_workspace_size", "ttj_int8_attn_layer_fwd",
@@ -67,6 +67,7 @@ _SIGNATURES = {
     "ttj_read_status": (ci, [vp, C.POINTER(ci), vp]),
     "ttj_selftest_wait_timeout": (ci, [vp, i64, vp]),
     "ttj_linear_fwd": (ci, [vp, vp, vp, vp, vp, vp, i64, i64, i64, ci, vp, vp]),
+    "ttj_linear_kchunked_fwd": (ci, [vp, i64, vp, vp, vp, vp, vp, i64, i64, i64, ci, vp, vp]),
     "ttj_qkv_proj_fwd": (ci, [vp, vp, vp, vp, i64, i64, ci, vp, vp]),
     "ttj_flash_attn_fwd": (ci, [vp, vp, vp, i64, i64, i64, i64, ci, ci, vp, vp]),
     "ttj_out_proj_residual_fwd": (ci, [vp, vp, vp, vp, vp, vp, i64, i64, ci, vp, vp]),

@@ -173,6 +173,37 @@ int ttj_linear_fwd(const void* x, const void* w, const void* bias, const void* r
   return ttj::launch_gemm(g, (cudaStream_t)stream);
 }
 
+int ttj_linear_kchunked_fwd(const void* x_chunks, int64_t k_chunk, const void* w, const void* bias,
+                            const void* residual, const uint8_t* row_mask, void* y, int64_t m,
+                            int64_t n, int64_t k, int dtype, int* status, ttj_stream_t stream) {
+  if (int rc = check_dtype(dtype)) return rc;
+  TTJ_CHECK_ARG(x_chunks && w && bias && y, TTJ_ERR_INVALID_ARG, "x_chunks, w, bias and y must be non-NULL");
+  TTJ_CHECK_ARG(m > 0 && n > 0 && k > 0 && k_chunk > 0, TTJ_ERR_INVALID_ARG, "m, n, k, k_chunk must be positive");
+  TTJ_CHECK_ARG(k_chunk % 64 == 0 && k % k_chunk == 0, TTJ_ERR_UNSUPPORTED,
+                "k_chunk must be a multiple of 64 that divides k");
+  TTJ_CHECK_ARG(n % 32 == 0, TTJ_ERR_UNSUPPORTED, "n must be a multiple of 32");
+  TTJ_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), TTJ_ERR_UNSUPPORTED, "dimension too large");
+  TTJ_CHECK_ARG(aligned16(x_chunks) && aligned16(w) && aligned16(bias) && aligned16(y) &&
+                    (residual == nullptr || aligned16(residual)),
+                TTJ_ERR_ALIGNMENT, "pointers must be 16-byte aligned");
+  ttj::GemmArgs g{};
+  g.a = x_chunks;
+  g.a_kchunk = k_chunk;
+  g.b = w;
+  g.bias = bias;
+  g.residual = residual;
+  g.row_mask = row_mask;
+  g.out = y;
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.in_dtype = dtype;
+  g.out_dtype = dtype;
+  g.epi = residual ? ttj::Epi::kBiasResidual : ttj::Epi::kBias;
+  g.status = status;
+  return ttj::launch_gemm(g, (cudaStream_t)stream);
+}
+
 int ttj_qkv_proj_fwd(const void* x, const void* w_qkv, const void* b_qkv, void* qkv,
                      int64_t tokens, int64_t d_model, int dtype, int* status, ttj_stream_t stream) {
   return ttj_linear_fwd(x, w_qkv, b_qkv, nullptr, nullptr, qkv, tokens, 3 * d_model, d_model, dtype,

@@ -43,6 +43,7 @@ constexpr int kBarrierBytes = 512;
 
 struct GemmParams {
   int M, N, K;
+  int a_kchunk;  // > 0: A is K-chunk-major [K/a_kchunk][M][a_kchunk] (3-D tensor map)
   int num_m_blocks, num_n_blocks;
   const void* bias;
   const uint8_t* row_mask;
@@ -307,7 +308,11 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             break;
           }
           mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes);
-          tma_load_2d(sA + stage * kABytes, &tmA, &full[stage], kb * kBK, m_blk * kBM);
+          if (p.a_kchunk > 0)
+            tma_load_3d(sA + stage * kABytes, &tmA, &full[stage], (kb * kBK) % p.a_kchunk, m_blk * kBM,
+                        (kb * kBK) / p.a_kchunk);
+          else
+            tma_load_2d(sA + stage * kABytes, &tmA, &full[stage], kb * kBK, m_blk * kBM);
           tma_load_2d(sB + stage * kBBytes, &tmB, &full[stage], kb * kBK, n_blk * BN);
           if (++stage == STAGES) {
             stage = 0;
@@ -487,8 +492,12 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           }
           const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
-          tma_load_2d_pair(sA + stage * kABytes, &tmA, leader_full, kb * kBK,
-                           m_blk * 2 * kBM + (int)rank * kBM);
+          if (p.a_kchunk > 0)
+            tma_load_3d_pair(sA + stage * kABytes, &tmA, leader_full, (kb * kBK) % p.a_kchunk,
+                             m_blk * 2 * kBM + (int)rank * kBM, (kb * kBK) / p.a_kchunk);
+          else
+            tma_load_2d_pair(sA + stage * kABytes, &tmA, leader_full, kb * kBK,
+                             m_blk * 2 * kBM + (int)rank * kBM);
           tma_load_2d_pair(sB + stage * kBBytes, &tmB, leader_full, kb * kBK,
                            n_blk * BN + (int)rank * (BN / 2));
           if (++stage == STAGES) {
@@ -587,7 +596,14 @@ int make_maps(const GemmArgs& g, int box_a_rows, int box_b_rows, CUtensorMap* ta
               CUtensorMap* tout, CUtensorMap* tres) {
   constexpr int kBK = kRowBytes / sizeof(TIn);
   const CUtensorMapDataType dt = tmap_dtype<TIn>();
-  {
+  if (g.a_kchunk > 0) {
+    // A(m, k) = a[k / kc][m][k % kc]: a 3-D map, one K-chunk per z.
+    const uint64_t kc = (uint64_t)g.a_kchunk;
+    const uint64_t dims[3] = {kc, (uint64_t)g.m, (uint64_t)g.k / kc};
+    const uint64_t strides[2] = {kc * sizeof(TIn), kc * (uint64_t)g.m * sizeof(TIn)};
+    const uint32_t box[3] = {(uint32_t)kBK, (uint32_t)box_a_rows, 1};
+    if (int rc = encode_tmap(ta, dt, 3, g.a, dims, strides, box)) return rc;
+  } else {
     const uint64_t dims[2] = {(uint64_t)g.k, (uint64_t)g.m};
     const uint64_t strides[1] = {(uint64_t)g.k * sizeof(TIn)};
     const uint32_t box[2] = {(uint32_t)kBK, (uint32_t)box_a_rows};
@@ -622,6 +638,7 @@ GemmParams make_params(const GemmArgs& g, int tile_m, int bn) {
   p.M = (int)g.m;
   p.N = (int)g.n;
   p.K = (int)g.k;
+  p.a_kchunk = (int)g.a_kchunk;
   p.num_m_blocks = (int)((g.m + tile_m - 1) / tile_m);
   p.num_n_blocks = (int)((g.n + bn - 1) / bn);
   p.bias = g.bias;

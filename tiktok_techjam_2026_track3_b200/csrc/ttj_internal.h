@@ -49,7 +49,7 @@ enum class Epi : int {
 };
 
 struct GemmArgs {
-  const void* a;          // [M, K]
+  const void* a;          // [M, K], or [K / a_kchunk][M][a_kchunk] when a_kchunk > 0
   const void* b;          // [N, K]
   const void* bias;       // [N]  (16-bit for kBias*, fp32 for kDequant*)
   const void* residual;   // [M, N]
@@ -62,6 +62,7 @@ struct GemmArgs {
   int out_dtype;          // TTJ_F16 / TTJ_BF16 (ignored for kRawS32)
   Epi epi;
   int* status;
+  int64_t a_kchunk = 0;   // > 0: A is stored K-chunk-major (see above); multiple of 64
 };
 int launch_gemm(const GemmArgs& g, cudaStream_t stream);
 

@@ -99,6 +99,32 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
     return y
 
 
+def linear_kchunked(x_chunks: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+                    residual: Optional[torch.Tensor] = None,
+                    row_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[m, :] = sum_c x_chunks[c, m, :] . w[:, c*kc:(c+1)*kc]^T + bias (+ residual):
+    the linear layer on an input stored K-chunk-major [K/kc, M, kc]."""
+    lib = _lib.load()
+    x_chunks, w, bias = _cuda(x_chunks, "x_chunks"), _cuda(w, "w"), _cuda(bias, "bias")
+    dt = _dtype_code(x_chunks)
+    nck, m, kc = x_chunks.shape
+    n, k = w.shape
+    if nck * kc != k:
+        raise RuntimeError("x_chunks chunks * chunk width must equal w's input features")
+    if residual is not None:
+        residual = _cuda(residual, "residual")
+    rm = None
+    if row_mask is not None:
+        rm = _cuda(row_mask.reshape(-1), "row_mask")
+        rm = rm.view(torch.uint8) if rm.dtype == torch.bool else (rm != 0).view(torch.uint8)
+    y = torch.empty(m, n, dtype=x_chunks.dtype, device=x_chunks.device)
+    rc = lib.ttj_linear_kchunked_fwd(x_chunks.data_ptr(), kc, w.data_ptr(), bias.data_ptr(),
+                                     _ptr(residual), _ptr(rm), y.data_ptr(), m, n, k, dt,
+                                     status_word(x_chunks.device).data_ptr(), _stream(x_chunks.device))
+    _lib.check(rc, "ttj_linear_kchunked_fwd")
+    return y
+
+
 def qkv_proj(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor) -> torch.Tensor:
     """[B,S,D] -> packed [B,S,3D] (q | k | v)."""
     lib = _lib.load()
@@ -114,15 +140,21 @@ def qkv_proj(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor) -> torch
 
 
 def flash_attn(qkv: torch.Tensor, num_heads: int, causal: bool,
-               key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Packed [B,S,3D] -> context [B,S,D] (heads merged)."""
+               key_mask: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Packed [B,S,3D] -> context [B,S,D] (heads merged), optionally into ``out``."""
     lib = _lib.load()
     qkv = _cuda(qkv, "qkv")
     dt = _dtype_code(qkv)
     B, S, D3 = qkv.shape
     D = D3 // 3
     km = _mask_u8(key_mask, B, S)
-    ctx = torch.empty(B, S, D, dtype=qkv.dtype, device=qkv.device)
+    if out is None:
+        ctx = torch.empty(B, S, D, dtype=qkv.dtype, device=qkv.device)
+    else:
+        if out.shape != (B, S, D) or out.dtype != qkv.dtype or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous [B,S,D] tensor of qkv's dtype")
+        ctx = out
     rc = lib.ttj_flash_attn_fwd(qkv.data_ptr(), _ptr(km), ctx.data_ptr(), B, S, num_heads,
                                 D // num_heads, int(bool(causal)), dt,
                                 status_word(qkv.device).data_ptr(), _stream(qkv.device))
