@@ -145,7 +145,10 @@ class ShardedAttention:
                 global_batch: Optional[int] = None):
         if self.mode == "heads":
             return self._forward_heads(x, valid_token_mask, causal)
-        out = self.backend.layer(self.layer, x, valid_token_mask, causal)
+        if x.shape[0] == 0:  # more ranks than batch rows: nothing to compute here
+            out = x.new_empty(x.shape)
+        else:
+            out = self.backend.layer(self.layer, x, valid_token_mask, causal)
         if not gather:
             return out
         if global_batch is None:
