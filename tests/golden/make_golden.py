@@ -11,7 +11,8 @@ What it imports from the reference, unmodified:
   ``generate_random_case`` (seeded inputs and prefix masks) and
   ``compare_outputs`` is not needed (fixtures store raw tensors);
 * ``Project/kernels/k008_int8_gemm.py``: ``_quant_rows``, ``_int8_pack`` and
-  ``_int8_linear`` (the W8A8 recipe).
+  ``_int8_linear`` (the W8A8 recipe);
+* ``BaselineTransformer`` for one whole-model fixture (``block_model.pt``).
 
 Each attention fixture stores the reference's inputs, the state dict it was
 run with, and the reference output ``x + attention(x, mask, causal)`` (the
@@ -76,6 +77,28 @@ def make_attention_fixture(ref, name, B, S, D, H, causal, padding, seed):
     }
 
 
+def make_block_fixture(ref, seed=2024):
+    """A 2-layer BaselineTransformer (the whole reference model) on a small shape."""
+    cfg = ref.TransformerConfig(batch_size=2, seq_len=96, d_model=128, num_heads=2, ffn_dim=256,
+                                num_layers=2, causal=True)
+    torch.manual_seed(seed)
+    model = ref.BaselineTransformer(cfg).eval()
+    g = torch.Generator().manual_seed(seed)
+    sd = {}
+    for k, v in model.state_dict().items():
+        if k.endswith("norm1.weight") or k.endswith("norm2.weight") or k == "final_norm.weight":
+            sd[k] = 1.0 + 0.1 * torch.randn(v.shape, generator=g)
+        else:
+            sd[k] = torch.randn(v.shape, generator=g) * 0.05
+    model.load_state_dict(sd, strict=True)
+    x, mask = ref.generate_random_case(cfg, torch.device("cpu"), torch.float32, seed, 0.25, 1.0)
+    with torch.inference_mode():
+        out = model(x, mask)
+    return {"config": dict(batch_size=2, seq_len=96, d_model=128, num_heads=2, ffn_dim=256,
+                           num_layers=2, causal=True),
+            "x": x, "mask": mask, "state_dict": sd, "out": out}
+
+
 def make_int8_fixture(k8, seed=4321, tokens=64, d_in=256, d_out=192):
     g = torch.Generator().manual_seed(seed)
     lin = torch.nn.Linear(d_in, d_out)
@@ -112,6 +135,9 @@ def main() -> int:
         fx = make_attention_fixture(ref, *case)
         torch.save(fx, HERE / f"attn_{case[0]}.pt")
         print("wrote", f"attn_{case[0]}.pt", tuple(fx["out"].shape))
+    fx = make_block_fixture(ref)
+    torch.save(fx, HERE / "block_model.pt")
+    print("wrote block_model.pt", tuple(fx["out"].shape))
     fx = make_int8_fixture(k8)
     torch.save(fx, HERE / "int8_recipe.pt")
     print("wrote int8_recipe.pt", tuple(fx["acc"].shape))

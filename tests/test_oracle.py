@@ -129,3 +129,15 @@ def test_int8_recipe_bit_exact(golden_dir):
     assert torch.equal(int_gemm_ref(a8, w8), fx["acc"])
     y = int8_linear_ref(fx["h"], w8, s_w, fx["bias"])
     assert torch.equal(y, fx["y"])
+
+
+def test_block_oracle_matches_reference_model(golden_dir):
+    """The whole-model restatement (blocks + final norm) against the reference's
+    BaselineTransformer output."""
+    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef
+    fx = torch.load(golden_dir / "block_model.pt", weights_only=False)
+    model = BaselineTransformerRef(TransformerConfigRef(**fx["config"]))
+    model.load_state_dict(fx["state_dict"], strict=True)
+    with torch.inference_mode():
+        out = model(fx["x"], fx["mask"])
+    torch.testing.assert_close(out, fx["out"], rtol=1e-5, atol=1e-5)

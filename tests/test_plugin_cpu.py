@@ -1,0 +1,25 @@
+"""The harness-facing drop-in without a GPU: module tree and state-dict keys
+equal the reference model's, strict load_state_dict works."""
+
+import types
+
+import torch
+
+from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef
+from tiktok_techjam_2026_track3_b200 import plugin
+
+
+def test_build_keeps_reference_state_dict(golden_dir):
+    fx = torch.load(golden_dir / "block_model.pt", weights_only=False)
+    cfg = TransformerConfigRef(**fx["config"])
+    otb = types.SimpleNamespace(BaselineTransformer=BaselineTransformerRef)
+    model = plugin.build(otb, cfg)
+    assert type(model).__name__ == "UserOptimizedTransformer"
+    assert isinstance(model, BaselineTransformerRef)
+    ref = BaselineTransformerRef(cfg)
+    assert list(model.state_dict().keys()) == list(ref.state_dict().keys())
+    model.load_state_dict(fx["state_dict"], strict=True)
+    # the attention view shares the block's Linear modules and adds no keys
+    attn = plugin.attention_sublayer(model.layers[0])
+    assert attn.q_proj is model.layers[0].attention.q_proj
+    assert list(model.state_dict().keys()) == list(ref.state_dict().keys())

@@ -31,6 +31,15 @@ from . import ops
 __all__ = ["B200SelfAttention", "B200AttentionLayer"]
 
 
+def _version(t: torch.Tensor) -> int:
+    """In-place modification counter; inference tensors have none (they cannot be
+    modified outside inference mode), so their storage address alone keys the cache."""
+    try:
+        return t._version
+    except RuntimeError:
+        return -1
+
+
 class B200SelfAttention(nn.Module):
     """sm_100a multi-head self-attention with the reference module's interface."""
 
@@ -60,7 +69,7 @@ class B200SelfAttention(nn.Module):
     def packed_weights(self) -> Tuple[torch.Tensor, ...]:
         """(w_qkv, b_qkv, w_o, b_o) or, for int8, (w_qkv8, s_qkv, b_qkv32, w_o8, s_o, b_o32)."""
         ps = self._params()
-        key = tuple((p.data_ptr(), p._version, p.dtype, p.device) for p in ps)
+        key = tuple((p.data_ptr(), _version(p), p.dtype, p.device) for p in ps)
         if key != self._pack_key or self._packed is None:
             with torch.no_grad():
                 wq, bq, wk, bk, wv, bv, wo, bo = (p.detach() for p in ps)
