@@ -9,12 +9,13 @@
 // A and B that share every K/V tile.  One CTA per SM loops over work items,
 // heaviest (longest causal key range) first.
 //
-// Roles (352 threads = 11 warps):
+// Roles (384 threads = 12 warps = 3 warpgroups):
 //   warp 0       TMA: K_j / V_j tiles into KV_STAGES-deep rings, item after item
 //   warp 1       MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j
 //                with P read from TMEM (tcgen05 "ts" form)
 //   warp 2       TMA: the two Q tiles of each work item
-//   warps 3..6   softmax for tile A, warps 7..10 for tile B: thread = query row;
+//   warp 3       idle (completes the first warpgroup)
+//   warps 4..7   softmax for tile A, warps 8..11 for tile B: thread = query row;
 //                load the S row from TMEM, mask, online softmax in fp32 with a
 //                lazily moved row max, write P (input dtype) to TMEM, rescale its
 //                O row when the max moved, and at the end normalise O and store
@@ -25,10 +26,12 @@
 // head_dim 64 ("separate P"): S_A [0,128) S_B [128,256) P_A [256,320)
 //   P_B [320,384) O_A [384,448) O_B [448,512).  S_t(j+1) = Q_t K_{j+1}^T is
 //   issued as soon as the softmax has read S_t(j) out of TMEM, so it is ready
-//   when the softmax finishes tile j; P_t(j) goes to its own buffer once
-//   P_t(j-1) V_{j-1} has completed (o_done).  The softmax never waits for the
-//   tensor core in steady state (measured: with P written over S the softmax
-//   idled ~40% of each step waiting for the P.V -> Q.K round trip).
+//   when the softmax finishes tile j.  P_t(j) is computed into registers and
+//   stored to its own buffer only then, after P_t(j-1) V_{j-1} has completed
+//   (o_done): that product was issued a whole softmax step earlier, so in
+//   steady state the softmax waits for neither S nor O (measured: with P
+//   written over S the softmax idled ~40% of each step on the P.V -> Q.K round
+//   trip; waiting for o_done before the exponentials cost ~15%).
 // head_dim 128 ("P over S"): S_A [0,128) S_B [128,256) O_A [256,384)
 //   O_B [384,512); P_t overwrites the first 64 columns of S_t, so the issue
 //   order per tile is PV_t(j-1), QK_t(j), commit s_full_t.  tcgen05.commit
@@ -43,7 +46,14 @@ namespace {
 constexpr int kBM = 128;     // queries per tile
 constexpr int kBN = 128;     // keys per KV tile
 constexpr int kChunkBytes = 128 * 128;  // one [128 rows][64 cols] 16-bit swizzled box
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
+// Register split (setmaxnreg): the block launches with kLaunchRegs per thread;
+// the first warpgroup (producers, MMA issuer) gives registers back to the two
+// softmax warpgroups.  128 * (kRegsCtl + 2 * kRegsSoftmax) == 384 * kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr uint32_t kRegsCtl = 88;
+constexpr uint32_t kRegsSoftmax = 208;
+static_assert(kRegsCtl + 2 * kRegsSoftmax == 3 * kLaunchRegs, "register split must use the launch budget");
 constexpr uint32_t kTmemCols = 512;
 
 struct AttnParams {
@@ -77,19 +87,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Two fp16 exponentials in one MUFU operation, result already packed for P.
-__device__ __forceinline__ uint32_t exp2_h2(uint32_t x2) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x2));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 // sm_100 packed fp32 pairs (two lanes per instruction) and 3-input max.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;
@@ -115,8 +112,16 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// The k-th work item of this CTA: item indices are dealt out in rounds of
+// gridDim.x, alternating direction each round ("snake" order).  With items
+// sorted heaviest first this keeps the per-CTA totals within ~3% of the mean
+// for causal attention (plain striding: ~11% for BASELINE config 2).
+__device__ __forceinline__ int item_of(int k) {
+  return k * (int)gridDim.x + ((k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
+}
+
 // Decode work item -> (b, h, pair).  Causal items are ordered by decreasing
-// pair index (longest key range first) so static striding balances the SMs.
+// pair index (longest key range first).
 struct Item {
   int b, h, pair;
 };
@@ -158,9 +163,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* q_full = bars;              // [1]
-  uint64_t* q_empty = q_full + 1;       // [1]
-  uint64_t* k_full = q_empty + 1;       // [ST]
+  uint64_t* q_full = bars;              // [2] per tile: Q_t loaded
+  uint64_t* q_empty = q_full + 2;       // [2] per tile: last Q_t K^T of the item done
+  uint64_t* k_full = q_empty + 2;       // [ST]
   uint64_t* k_empty = k_full + ST;      // [ST]
   uint64_t* v_full = k_empty + ST;      // [ST]
   uint64_t* v_empty = v_full + ST;      // [ST]
@@ -176,8 +181,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -185,6 +188,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
       mbar_init(&v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
       mbar_init(&s_full[t], 1);
       mbar_init(&s_free[t], 128);
       mbar_init(&p_full[t], 128);
@@ -204,173 +209,215 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ K/V producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tm);
-      int kv = 0;  // running K/V tile counter across items
-      bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
-        const Item it = decode_item<CAUSAL>(item, p);
-        const int n_kv = kv_tiles<CAUSAL>(it.pair, 1, p.S);
-        const int xk = p.D + it.h * HD, xv = 2 * p.D + it.h * HD;
-        for (int j = 0; j < n_kv; ++j, ++kv) {
-          const int st = kv % ST;
-          const uint32_t ph = (kv / ST) & 1;
-          if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
-          for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, it.b);
-          if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
-          for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, it.b);
-        }
-      }
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ Q producer
-    if (lane == 0) {
-      int k = 0;
-      for (int item = blockIdx.x; item < p.num_items; item += gridDim.x, ++k) {
-        const Item it = decode_item<CAUSAL>(item, p);
-        if (!mbar_wait(q_empty, (k & 1) ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(q_full, 2 * L::kTileBytes);
-        for (int t = 0; t < 2; ++t)
-          for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sQ + t * L::kTileBytes + c * kChunkBytes, &tm, q_full, it.h * HD + 64 * c,
-                        it.pair * 2 * kBM + t * kBM, it.b);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      int kv = 0, k = 0;
-      uint32_t pf_phase[2] = {0u, 0u};
-      uint32_t sfree_phase[2] = {0u, 0u};
-      int qk_count[2] = {0, 0};
-      bool ok = true;
-      auto qk = [&](int t, int st) {
-        const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
-        const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem + t * 128, smem_desc_sw128(q_addr + off, 16, 1024),
-                      smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto pv = [&](int t, int st, bool accumulate) {
-        const uint32_t v_addr = smem_u32(sV + st * L::kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // V is MN-major: 16 keys = 16 rows of 128 bytes; next 64-column chunk at +16 KB.
-          umma_f16_ts(tmem + L::kColO + t * HD, tmem + L::kColP + t * kPStride + kk * 8,
-                      smem_desc_sw128(v_addr + kk * 16 * 128, kChunkBytes, 1024), kIdescPV,
-                      (accumulate || kk > 0) ? 1u : 0u);
-        }
-      };
-      // Separate-P schedule: QK_t may overwrite S_t once the softmax has read the
-      // previous S_t (s_free), including the last one of the previous item.
-      auto issue_qk_sep = [&](int t, int st) -> bool {
-        if (qk_count[t] > 0) {
-          if (!mbar_wait(&s_free[t], sfree_phase[t], p.status, kDevTimeoutSoftmax, abort_flag)) return false;
-          sfree_phase[t] ^= 1u;
-        }
-        tc_fence_after();
-        qk(t, st);
-        umma_commit(&s_full[t]);
-        ++qk_count[t];
-        return true;
-      };
-      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++k) {
-        const Item it = decode_item<CAUSAL>(item, p);
-        const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
-        const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);  // n_b >= n_a
-        if (!mbar_wait(q_full, k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-        const int kv0 = kv;
-        // prologue: S_A(0), S_B(0)
-        {
-          const int st = kv0 % ST;
-          if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-          if constexpr (kSepP) {
-            if (!issue_qk_sep(0, st) || !issue_qk_sep(1, st)) break;
-          } else {
-            tc_fence_after();
-            qk(0, st);
-            umma_commit(&s_full[0]);
-            qk(1, st);
-            umma_commit(&s_full[1]);
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsCtl>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ K/V producer
+      if (lane == 0) {
+        tma_prefetch_desc(&tm);
+        int kv = 0;  // running K/V tile counter across items
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+          const int item = item_of(k);
+          if (item >= p.num_items) break;
+          const Item it = decode_item<CAUSAL>(item, p);
+          const int n_kv = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+          const int xk = p.D + it.h * HD, xv = 2 * p.D + it.h * HD;
+          for (int j = 0; j < n_kv; ++j, ++kv) {
+            const int st = kv % ST;
+            const uint32_t ph = (kv / ST) & 1;
+            if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
+            for (int c = 0; c < kChunks; ++c)
+              tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, it.b);
+            if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
+            for (int c = 0; c < kChunks; ++c)
+              tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, it.b);
           }
-          umma_commit(&k_empty[st]);
-          if (n_b == 1) umma_commit(q_empty);
         }
-        for (int j = 0; j < n_b; ++j) {
-          const int st = (kv0 + j) % ST;
-          const uint32_t ph = ((kv0 + j) / ST) & 1;
-          const int st_n = (kv0 + j + 1) % ST;
-          const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
-          const bool next_b = j + 1 < n_b;
-          if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-          if constexpr (kSepP) {
-            // next scores first, then this step's P.V products
-            if (next_b) {
-              if (j + 1 < n_a && !issue_qk_sep(0, st_n)) { ok = false; break; }
-              if (!issue_qk_sep(1, st_n)) { ok = false; break; }
-              umma_commit(&k_empty[st_n]);
-              if (j + 2 == n_b) umma_commit(q_empty);  // last QK of the item issued
+      }
+    } else if (warp == 2) {
+      // ------------------------------------------------------------ Q producer
+      if (lane == 0) {
+        for (int k = 0;; ++k) {
+          const int item = item_of(k);
+          if (item >= p.num_items) break;
+          const Item it = decode_item<CAUSAL>(item, p);
+          bool ok = true;
+          for (int t = 0; t < 2 && ok; ++t) {
+            ok = mbar_wait(&q_empty[t], (k & 1) ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&q_full[t], L::kTileBytes);
+            for (int c = 0; c < kChunks; ++c)
+              tma_load_3d(sQ + t * L::kTileBytes + c * kChunkBytes, &tm, &q_full[t], it.h * HD + 64 * c,
+                          it.pair * 2 * kBM + t * kBM, it.b);
+          }
+          if (!ok) break;
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        auto qk = [&](int t, int st) {
+          const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
+          const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
+  #pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+            umma_f16_ss(tmem + t * 128, smem_desc_sw128(q_addr + off, 16, 1024),
+                        smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+          }
+        };
+        auto pv = [&](int t, int st, bool accumulate) {
+          const uint32_t v_addr = smem_u32(sV + st * L::kTileBytes);
+  #pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            // V is MN-major: 16 keys = 16 rows of 128 bytes; next 64-column chunk at +16 KB.
+            umma_f16_ts(tmem + L::kColO + t * HD, tmem + L::kColP + t * kPStride + kk * 8,
+                        smem_desc_sw128(v_addr + kk * 16 * 128, kChunkBytes, 1024), kIdescPV,
+                        (accumulate || kk > 0) ? 1u : 0u);
+          }
+        };
+        if constexpr (kSepP) {
+          int kv = 0;
+          uint32_t pf_phase[2] = {0u, 0u};
+          uint32_t sfree_phase[2] = {0u, 0u};
+          int qk_count[2] = {0, 0};
+          bool ok = true;
+          auto issue_qk_sep = [&](int t, int st) -> bool {
+            if (qk_count[t] > 0) {
+              if (!mbar_wait(&s_free[t], sfree_phase[t], p.status, kDevTimeoutSoftmax, abort_flag)) return false;
+              sfree_phase[t] ^= 1u;
             }
-            if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-            if (j < n_a) {
-              if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-              pf_phase[0] ^= 1u;
-              tc_fence_after();
-              pv(0, st, j > 0);
-              umma_commit(&o_done[0]);
-            }
-            if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-            pf_phase[1] ^= 1u;
             tc_fence_after();
-            pv(1, st, j > 0);
-            umma_commit(&o_done[1]);
-            umma_commit(&v_empty[st]);
-          } else {
-            if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-            if (j < n_a) {
-              if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-              pf_phase[0] ^= 1u;
-              tc_fence_after();
-              pv(0, st, j > 0);
-              if (j + 1 < n_a) {
-                qk(0, st_n);
-                umma_commit(&s_full[0]);
-              } else {
+            qk(t, st);
+            umma_commit(&s_full[t]);
+            ++qk_count[t];
+            return true;
+          };
+          for (int k = 0; ok; ++k) {
+            const int item = item_of(k);
+            if (item >= p.num_items) break;
+            const Item it = decode_item<CAUSAL>(item, p);
+            const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
+            const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+            if (!mbar_wait(&q_full[0], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+            if (!mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+            const int kv0 = kv;
+            {
+              const int st = kv0 % ST;
+              if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+              if (!issue_qk_sep(0, st) || !issue_qk_sep(1, st)) break;
+              umma_commit(&k_empty[st]);
+              if (n_a == 1) umma_commit(&q_empty[0]);
+              if (n_b == 1) umma_commit(&q_empty[1]);
+            }
+            for (int j = 0; j < n_b; ++j) {
+              const int st = (kv0 + j) % ST;
+              const uint32_t ph = ((kv0 + j) / ST) & 1;
+              const int st_n = (kv0 + j + 1) % ST;
+              const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
+              const bool next_b = j + 1 < n_b;
+              if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+              if (next_b) {
+                if (j + 1 < n_a) {
+                  if (!issue_qk_sep(0, st_n)) { ok = false; break; }
+                  if (j + 2 == n_a) umma_commit(&q_empty[0]);
+                }
+                if (!issue_qk_sep(1, st_n)) { ok = false; break; }
+                umma_commit(&k_empty[st_n]);
+                if (j + 2 == n_b) umma_commit(&q_empty[1]);
+              }
+              if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+              if (j < n_a) {
+                if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+                pf_phase[0] ^= 1u;
+                tc_fence_after();
+                pv(0, st, j > 0);
                 umma_commit(&o_done[0]);
               }
-            }
-            if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-            pf_phase[1] ^= 1u;
-            tc_fence_after();
-            pv(1, st, j > 0);
-            umma_commit(&v_empty[st]);
-            if (next_b) {
-              qk(1, st_n);
-              umma_commit(&s_full[1]);
-              umma_commit(&k_empty[st_n]);
-              if (j + 2 == n_b) umma_commit(q_empty);
-            } else {
+              if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+              pf_phase[1] ^= 1u;
+              tc_fence_after();
+              pv(1, st, j > 0);
               umma_commit(&o_done[1]);
+              umma_commit(&v_empty[st]);
             }
+            kv = kv0 + n_b;
+          }
+        } else {
+          int kv = 0;
+          uint32_t pf_phase[2] = {0u, 0u};
+          bool ok = true;
+          for (int k = 0; ok; ++k) {
+            const int item = item_of(k);
+            if (item >= p.num_items) break;
+            const Item it = decode_item<CAUSAL>(item, p);
+            const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
+            const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);  // n_b >= n_a
+            if (!mbar_wait(&q_full[0], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+            if (!mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+            const int kv0 = kv;
+            // prologue: S_A(0), S_B(0)
+            {
+              const int st = kv0 % ST;
+              if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+              tc_fence_after();
+              qk(0, st);
+              umma_commit(&s_full[0]);
+              if (n_a == 1) umma_commit(&q_empty[0]);
+              qk(1, st);
+              umma_commit(&s_full[1]);
+              if (n_b == 1) umma_commit(&q_empty[1]);
+              umma_commit(&k_empty[st]);
+            }
+            for (int j = 0; j < n_b; ++j) {
+              const int st = (kv0 + j) % ST;
+              const uint32_t ph = ((kv0 + j) / ST) & 1;
+              const int st_n = (kv0 + j + 1) % ST;
+              const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
+              const bool next_b = j + 1 < n_b;
+              if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+              if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+              if (j < n_a) {
+                if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+                pf_phase[0] ^= 1u;
+                tc_fence_after();
+                pv(0, st, j > 0);
+                if (j + 1 < n_a) {
+                  qk(0, st_n);
+                  umma_commit(&s_full[0]);
+                  if (j + 2 == n_a) umma_commit(&q_empty[0]);
+                } else {
+                  umma_commit(&o_done[0]);
+                }
+              }
+              if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+              pf_phase[1] ^= 1u;
+              tc_fence_after();
+              pv(1, st, j > 0);
+              umma_commit(&v_empty[st]);
+              if (next_b) {
+                qk(1, st_n);
+                umma_commit(&s_full[1]);
+                umma_commit(&k_empty[st_n]);
+                if (j + 2 == n_b) umma_commit(&q_empty[1]);
+              } else {
+                umma_commit(&o_done[1]);
+              }
+            }
+            kv = kv0 + n_b;
           }
         }
-        kv = kv0 + n_b;
+        umma_commit(drain);
+        mbar_wait(drain, 0, p.status, kDevTimeoutSoftmax, nullptr);
       }
-      umma_commit(drain);
-      mbar_wait(drain, 0, p.status, kDevTimeoutSoftmax, nullptr);
     }
-  } else if (warp >= 3) {
+  } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax (tile A or B)
-    const int t = warp >= 7 ? 1 : 0;
+    const int t = warp >= 8 ? 1 : 0;
     const int lg = warp & 3;             // TMEM lane quarter of this warp
     const int r = lg * 32 + lane;        // query row within the tile
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(lg * 32) << 16);
@@ -380,7 +427,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     uint32_t sf_phase = 0;
     uint32_t od_phase = 0;  // o_done parity of the next P.V to wait for
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
+    for (int k = 0; ok; ++k) {
+      const int item = item_of(k);
+      if (item >= p.num_items) break;
       const Item it = decode_item<CAUSAL>(item, p);
       const int n_kv = kv_tiles<CAUSAL>(it.pair, t, p.S);
       const int q0 = it.pair * 2 * kBM + t * kBM;
@@ -442,68 +491,48 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
         const float m_new = (m_tile > m_run + 8.f) ? m_tile : m_run;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
         const float alpha = fast_exp2(m_run - m_use);  // 1 unchanged, 0 from -inf
-        if (kSepP && j > 0) {
-          // P_t(j-1) V must have completed: it read the P buffer written below
-          // and it is the last write to O_t before a rescale.  It was issued
-          // about one softmax step ago, so this wait is normally free.
-          if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-          od_phase ^= 1u;
-          tc_fence_after();
-        }
-        // x = s * scale_log2 - m as packed pairs; P = 2^x, written to TMEM 16
-        // columns (32 keys) at a time: its own buffer, or over the S columns
-        // already read.
+        // x = s * scale_log2 - m as packed pairs; P = 2^x.  Written over the S
+        // columns already read 16 columns (32 keys) at a time, or, with separate
+        // P buffers, kept in registers and stored after the wait below.
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
         const uint64_t nm2 = f2_pack(-m_use, -m_use);
-        float sum;
-        if constexpr (!kBf16) {
-          // fp16: x <= 8, so 2^x <= 256 fits fp16; exponentials two per MUFU op,
-          // row sums accumulated as fp16 pairs in 16 short chains (<= 4 adds
-          // each), finished in fp32.
-          uint32_t hs[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        // One MUFU exponential per element in fp32 (measured faster than the
+        // paired fp16 form, which issues half the instructions but at half rate),
+        // row sums as fp32 pairs in four chains.
+        uint32_t pk[2][32];
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-          for (int c = 0; c < kBN / 32; ++c) {
-            uint32_t pk[16];
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t (&pc)[16] = *reinterpret_cast<uint32_t(*)[16]>(&pk[c >> 1][(c & 1) * 16]);
 #pragma unroll
-            for (int ii = 0; ii < 16; ++ii) {
-              const int i = c * 16 + ii;
-              float x0, x1;
-              f2_unpack(ffma2(f2_pack(s[2 * i], s[2 * i + 1]), c2, nm2), x0, x1);
-              pk[ii] = exp2_h2(Pack<__half>::two(x0, x1));
-              hs[i & 7] = (i < 8) ? pk[ii] : hadd2_u(hs[i & 7], pk[ii]);
-            }
-            tmem_st16(t_p + c * 16, pk);
+          for (int ii = 0; ii < 16; ++ii) {
+            const int i = c * 16 + ii;
+            float x0, x1;
+            f2_unpack(ffma2(f2_pack(s[2 * i], s[2 * i + 1]), c2, nm2), x0, x1);
+            const float e0 = fast_exp2(x0);
+            const float e1 = fast_exp2(x1);
+            pc[ii] = Pack<T>::two(e0, e1);
+            sum2[i & 3] = fadd2(sum2[i & 3], f2_pack(e0, e1));
           }
-          float acc = 0.f;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float2 f = Pack<__half>::unpack(hs[q]);
-            acc += f.x + f.y;
-          }
-          sum = acc;
-        } else {
-          uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-          for (int c = 0; c < kBN / 32; ++c) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int ii = 0; ii < 16; ++ii) {
-              const int i = c * 16 + ii;
-              float x0, x1;
-              f2_unpack(ffma2(f2_pack(s[2 * i], s[2 * i + 1]), c2, nm2), x0, x1);
-              const float e0 = fast_exp2(x0);
-              const float e1 = fast_exp2(x1);
-              pk[ii] = Pack<T>::two(e0, e1);
-              sum2[i & 3] = fadd2(sum2[i & 3], f2_pack(e0, e1));
-            }
-            tmem_st16(t_p + c * 16, pk);
-          }
-          float a0, a1;
-          f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), a0, a1);
-          sum = a0 + a1;
+          if constexpr (!kSepP) tmem_st16(t_p + c * 16, pc);
         }
+        float a0, a1;
+        f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), a0, a1);
+        const float sum = a0 + a1;
         l_run = l_run * alpha + sum;
         m_run = m_new;
+        if constexpr (kSepP) {
+          if (j > 0) {
+            // P_t(j-1) V must have completed: it reads the P buffer written here
+            // and it is the last write to O_t before a rescale.  It was issued a
+            // whole softmax step ago, so this wait is normally free.
+            if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            od_phase ^= 1u;
+            tc_fence_after();
+          }
+          tmem_st32(t_p, pk[0]);
+          tmem_st32(t_p + 32, pk[1]);
+        }
         // Rescale O_t when the exponent reference moved (O_t holds P(0..j-1) V).
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -547,7 +576,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
       // p_full arrival, which follows these loads.
     }
   }
-
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -580,6 +608,14 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
   p.status = a.status;
   auto kern = flash_fwd_kernel<T, HD, CAUSAL>;
+  {
+    // The register split inside the kernel assumes this launch allocation;
+    // with any other the softmax warps' setmaxnreg.inc could never complete.
+    cudaFuncAttributes fa;
+    TTJ_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+    if (fa.numRegs != kLaunchRegs)
+      return fail(TTJ_ERR_UNSUPPORTED, "attention kernel register count differs from its register split");
+  }
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
   const int grid = p.num_items < sm_count() ? p.num_items : sm_count();
   kern<<<grid, kThreads, L::kTotal, stream>>>(tm, p);
