@@ -11,10 +11,10 @@
 //
 // Roles (384 threads = 12 warps = 3 warpgroups):
 //   warp 0       TMA: K_j / V_j tiles into KV_STAGES-deep rings, item after item
-//   warp 1       MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j
-//                with P read from TMEM (tcgen05 "ts" form)
+//   warps 1, 3   MMA issue, one thread: S_t = Q_t K_j^T into TMEM, O_t += P_t V_j
+//                with P read from TMEM (tcgen05 "ts" form); head_dim 64: warp 1
+//                for tile A, warp 3 for tile B; head_dim 128: warp 1 for both
 //   warp 2       TMA: the two Q tiles of each work item
-//   warp 3       idle (completes the first warpgroup)
 //   warps 4..7   softmax for tile A, warps 8..11 for tile B: thread = query row;
 //                load the S row from TMEM, mask, online softmax in fp32 with a
 //                lazily moved row max, write P (input dtype) to TMEM, rescale its
@@ -166,15 +166,15 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   uint64_t* q_full = bars;              // [2] per tile: Q_t loaded
   uint64_t* q_empty = q_full + 2;       // [2] per tile: last Q_t K^T of the item done
   uint64_t* k_full = q_empty + 2;       // [ST]
-  uint64_t* k_empty = k_full + ST;      // [ST]
-  uint64_t* v_full = k_empty + ST;      // [ST]
-  uint64_t* v_empty = v_full + ST;      // [ST]
-  uint64_t* s_full = v_empty + ST;      // [2] per tile: S_t written
+  uint64_t* k_empty = k_full + ST;      // [2][ST] per tile: its Q_t K^T done with the stage
+  uint64_t* v_full = k_empty + 2 * ST;  // [ST]
+  uint64_t* v_empty = v_full + ST;      // [2][ST] per tile: its P_t V done with the stage
+  uint64_t* s_full = v_empty + 2 * ST;  // [2] per tile: S_t written
   uint64_t* s_free = s_full + 2;        // [2] per tile: S_t read by the softmax (separate P)
   uint64_t* p_full = s_free + 2;        // [2] per tile: P_t written
   uint64_t* o_done = p_full + 2;        // [2] per tile: one phase per completed P_t V
-  uint64_t* drain = o_done + 2;         // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_done + 2;         // [2] per tile: every MMA of its issuer completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -183,9 +183,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      for (int t = 0; t < 2; ++t) {
+        mbar_init(&k_empty[t * ST + s], 1);
+        mbar_init(&v_empty[t * ST + s], 1);
+      }
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&q_full[t], 1);
@@ -194,8 +196,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
       mbar_init(&s_free[t], 128);
       mbar_init(&p_full[t], 128);
       mbar_init(&o_done[t], 1);
+      mbar_init(&drain[t], 1);
     }
-    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -211,207 +213,230 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
 
   if (warp < 4) {
     setmaxnreg_dec<kRegsCtl>();
-    if (warp == 0) {
+    if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ K/V producer
-      if (lane == 0) {
-        tma_prefetch_desc(&tm);
-        int kv = 0;  // running K/V tile counter across items
+      // A stage is refilled once every tile that used its previous key tile has
+      // released it (tile A skips the last key tile of a causal item).  Bit st
+      // of pend[t]: tile t still holds stage st; bit st of ph[t]: parity of
+      // tile t's next release of it.
+      tma_prefetch_desc(&tm);
+      uint32_t kpend[2] = {0u, 0u}, kph[2] = {0u, 0u}, vpend[2] = {0u, 0u}, vph[2] = {0u, 0u};
+      auto reclaim = [&](uint64_t* empty, uint32_t (&pend)[2], uint32_t (&ph)[2], int st,
+                         uint32_t users) -> bool {
+        for (int t = 0; t < 2; ++t) {
+          if ((pend[t] >> st) & 1u) {
+            if (!mbar_wait(&empty[t * ST + st], (ph[t] >> st) & 1u, p.status, kDevTimeoutSmemEmpty, abort_flag))
+              return false;
+            ph[t] ^= 1u << st;
+          }
+          pend[t] = (pend[t] & ~(1u << st)) | (((users >> t) & 1u) << st);
+        }
+        return true;
+      };
+      int kv = 0;  // running K/V tile counter across items
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int item = item_of(k);
+        if (item >= p.num_items) break;
+        const Item it = decode_item<CAUSAL>(item, p);
+        const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
+        const int n_kv = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+        const int xk = p.D + it.h * HD, xv = 2 * p.D + it.h * HD;
+        for (int j = 0; j < n_kv; ++j, ++kv) {
+          const int st = kv % ST;
+          // bit t: tile t releases this key tile (with P over S one thread issues
+          // both tiles' products and releases through tile B's barrier)
+          const uint32_t users = (kSepP && j < n_a) ? 3u : 2u;
+          if (!reclaim(k_empty, kpend, kph, st, users)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, it.b);
+          if (!reclaim(v_empty, vpend, vph, st, users)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, it.b);
+        }
+      }
+    } else if (warp == 2 && lane == 0) {
+      // ------------------------------------------------------------ Q producer
+      for (int k = 0;; ++k) {
+        const int item = item_of(k);
+        if (item >= p.num_items) break;
+        const Item it = decode_item<CAUSAL>(item, p);
         bool ok = true;
+        for (int t = 0; t < 2 && ok; ++t) {
+          ok = mbar_wait(&q_empty[t], (k & 1) ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&q_full[t], L::kTileBytes);
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sQ + t * L::kTileBytes + c * kChunkBytes, &tm, &q_full[t], it.h * HD + 64 * c,
+                        it.pair * 2 * kBM + t * kBM, it.b);
+        }
+        if (!ok) break;
+      }
+    } else if (lane == 0 && (warp == 1 || (kSepP && warp == 3))) {
+      // ------------------------------------------------------------ MMA issue
+      auto qk = [&](int t, int st) {
+        const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
+        const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+          umma_f16_ss(tmem + t * 128, smem_desc_sw128(q_addr + off, 16, 1024),
+                      smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int t, int st, bool accumulate) {
+        const uint32_t v_addr = smem_u32(sV + st * L::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // V is MN-major: 16 keys = 16 rows of 128 bytes; next 64-column chunk at +16 KB.
+          umma_f16_ts(tmem + L::kColO + t * HD, tmem + L::kColP + t * kPStride + kk * 8,
+                      smem_desc_sw128(v_addr + kk * 16 * 128, kChunkBytes, 1024), kIdescPV,
+                      (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+      if constexpr (kSepP) {
+        // Separate P: one issuing thread per tile (warp 1: A, warp 3: B).
+        // Measured: one thread issuing both tiles' products, waits and commits
+        // spent the whole step on that serial work while the tensor pipe idled
+        // more than half of it.  Per tile the QK cursor runs one key tile ahead
+        // of the P.V cursor, across items: S_t(j+1) is issued once the softmax
+        // has read S_t(j) (s_free), then O_t += P_t(j) V_j once P_t(j) is written.
+        const int t = warp == 3 ? 1 : 0;
+        int qk_k = 0, qk_j = 0, qk_kv0 = 0, qk_n = 0, qk_nb = 0;
+        bool qk_first = true;
+        auto qk_open = [&]() -> bool {
+          const int item = item_of(qk_k);
+          if (item >= p.num_items) return false;
+          const Item it = decode_item<CAUSAL>(item, p);
+          qk_n = kv_tiles<CAUSAL>(it.pair, t, p.S);
+          qk_nb = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+          return true;
+        };
+        bool qk_live = qk_open();
+        uint32_t sfree_ph = 0u, pf_ph = 0u;
+        auto issue_qk = [&]() -> bool {
+          if (!qk_live) return true;
+          if (qk_j == 0 && !mbar_wait(&q_full[t], qk_k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) return false;
+          if (!qk_first) {
+            if (!mbar_wait(&s_free[t], sfree_ph, p.status, kDevTimeoutSoftmax, abort_flag)) return false;
+            sfree_ph ^= 1u;
+          }
+          const int kvi = qk_kv0 + qk_j;
+          const int st = kvi % ST;
+          if (!mbar_wait(&k_full[st], (kvi / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) return false;
+          tc_fence_after();
+          qk(t, st);
+          umma_commit(&s_full[t]);
+          umma_commit(&k_empty[t * ST + st]);
+          qk_first = false;
+          if (++qk_j == qk_n) {  // last S_t of the item: Q_t may be replaced
+            umma_commit(&q_empty[t]);
+            qk_kv0 += qk_nb;
+            qk_j = 0;
+            ++qk_k;
+            qk_live = qk_open();
+          }
+          return true;
+        };
+        bool ok = issue_qk();
+        int kv0 = 0;
         for (int k = 0; ok; ++k) {
           const int item = item_of(k);
           if (item >= p.num_items) break;
           const Item it = decode_item<CAUSAL>(item, p);
-          const int n_kv = kv_tiles<CAUSAL>(it.pair, 1, p.S);
-          const int xk = p.D + it.h * HD, xv = 2 * p.D + it.h * HD;
-          for (int j = 0; j < n_kv; ++j, ++kv) {
-            const int st = kv % ST;
-            const uint32_t ph = (kv / ST) & 1;
-            if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
-            mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
-            for (int c = 0; c < kChunks; ++c)
-              tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, it.b);
-            if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) { ok = false; break; }
-            mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
-            for (int c = 0; c < kChunks; ++c)
-              tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, it.b);
+          const int n = kv_tiles<CAUSAL>(it.pair, t, p.S);
+          const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+          for (int j = 0; j < n; ++j) {
+            if (!issue_qk()) { ok = false; break; }  // S_t(j+1) or the next item's S_t(0)
+            if (!mbar_wait(&p_full[t], pf_ph, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            pf_ph ^= 1u;
+            const int kvi = kv0 + j;
+            const int st = kvi % ST;
+            if (!mbar_wait(&v_full[st], (kvi / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            pv(t, st, j > 0);
+            umma_commit(&o_done[t]);
+            umma_commit(&v_empty[t * ST + st]);
           }
+          kv0 += n_b;
         }
-      }
-    } else if (warp == 2) {
-      // ------------------------------------------------------------ Q producer
-      if (lane == 0) {
-        for (int k = 0;; ++k) {
+        // Nothing of this thread's may still run on the tensor core when TMEM
+        // is released (matters only after an abort).
+        umma_commit(&drain[t]);
+        mbar_wait(&drain[t], 0, p.status, kDevTimeoutSoftmax, nullptr);
+      } else {
+        // P over S: one thread issues both tiles, PV_A(j) QK_A(j+1) PV_B(j)
+        // QK_B(j+1) (measured faster here than one thread per tile: each tile's
+        // next S waits for its own P.V, and the fixed interleave keeps the two
+        // tiles' softmax steps half a step apart).
+        int kv = 0;
+        uint32_t pf_phase[2] = {0u, 0u};
+        bool ok = true;
+        // One commit per stage, through tile B's barrier: it arrives once every
+        // earlier product of this thread (tile A's included) has completed.
+        auto release = [&](uint64_t* empty, int st) { umma_commit(&empty[ST + st]); };
+        for (int k = 0; ok; ++k) {
           const int item = item_of(k);
           if (item >= p.num_items) break;
           const Item it = decode_item<CAUSAL>(item, p);
-          bool ok = true;
-          for (int t = 0; t < 2 && ok; ++t) {
-            ok = mbar_wait(&q_empty[t], (k & 1) ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&q_full[t], L::kTileBytes);
-            for (int c = 0; c < kChunks; ++c)
-              tma_load_3d(sQ + t * L::kTileBytes + c * kChunkBytes, &tm, &q_full[t], it.h * HD + 64 * c,
-                          it.pair * 2 * kBM + t * kBM, it.b);
-          }
-          if (!ok) break;
-        }
-      }
-    } else if (warp == 1) {
-      // ------------------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        auto qk = [&](int t, int st) {
-          const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
-          const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
-  #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-            umma_f16_ss(tmem + t * 128, smem_desc_sw128(q_addr + off, 16, 1024),
-                        smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
-          }
-        };
-        auto pv = [&](int t, int st, bool accumulate) {
-          const uint32_t v_addr = smem_u32(sV + st * L::kTileBytes);
-  #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            // V is MN-major: 16 keys = 16 rows of 128 bytes; next 64-column chunk at +16 KB.
-            umma_f16_ts(tmem + L::kColO + t * HD, tmem + L::kColP + t * kPStride + kk * 8,
-                        smem_desc_sw128(v_addr + kk * 16 * 128, kChunkBytes, 1024), kIdescPV,
-                        (accumulate || kk > 0) ? 1u : 0u);
-          }
-        };
-        if constexpr (kSepP) {
-          int kv = 0;
-          uint32_t pf_phase[2] = {0u, 0u};
-          uint32_t sfree_phase[2] = {0u, 0u};
-          int qk_count[2] = {0, 0};
-          bool ok = true;
-          auto issue_qk_sep = [&](int t, int st) -> bool {
-            if (qk_count[t] > 0) {
-              if (!mbar_wait(&s_free[t], sfree_phase[t], p.status, kDevTimeoutSoftmax, abort_flag)) return false;
-              sfree_phase[t] ^= 1u;
-            }
+          const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
+          const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);  // n_b >= n_a
+          if (!mbar_wait(&q_full[0], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+          if (!mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+          const int kv0 = kv;
+          {
+            const int st = kv0 % ST;
+            if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
             tc_fence_after();
-            qk(t, st);
-            umma_commit(&s_full[t]);
-            ++qk_count[t];
-            return true;
-          };
-          for (int k = 0; ok; ++k) {
-            const int item = item_of(k);
-            if (item >= p.num_items) break;
-            const Item it = decode_item<CAUSAL>(item, p);
-            const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
-            const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);
-            if (!mbar_wait(&q_full[0], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-            if (!mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-            const int kv0 = kv;
-            {
-              const int st = kv0 % ST;
-              if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-              if (!issue_qk_sep(0, st) || !issue_qk_sep(1, st)) break;
-              umma_commit(&k_empty[st]);
-              if (n_a == 1) umma_commit(&q_empty[0]);
-              if (n_b == 1) umma_commit(&q_empty[1]);
-            }
-            for (int j = 0; j < n_b; ++j) {
-              const int st = (kv0 + j) % ST;
-              const uint32_t ph = ((kv0 + j) / ST) & 1;
-              const int st_n = (kv0 + j + 1) % ST;
-              const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
-              const bool next_b = j + 1 < n_b;
-              if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-              if (next_b) {
-                if (j + 1 < n_a) {
-                  if (!issue_qk_sep(0, st_n)) { ok = false; break; }
-                  if (j + 2 == n_a) umma_commit(&q_empty[0]);
-                }
-                if (!issue_qk_sep(1, st_n)) { ok = false; break; }
-                umma_commit(&k_empty[st_n]);
-                if (j + 2 == n_b) umma_commit(&q_empty[1]);
-              }
-              if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-              if (j < n_a) {
-                if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-                pf_phase[0] ^= 1u;
-                tc_fence_after();
-                pv(0, st, j > 0);
+            qk(0, st);
+            umma_commit(&s_full[0]);
+            if (n_a == 1) umma_commit(&q_empty[0]);
+            qk(1, st);
+            umma_commit(&s_full[1]);
+            if (n_b == 1) umma_commit(&q_empty[1]);
+            release(k_empty, st);
+          }
+          for (int j = 0; j < n_b; ++j) {
+            const int st = (kv0 + j) % ST;
+            const uint32_t ph = ((kv0 + j) / ST) & 1;
+            const int st_n = (kv0 + j + 1) % ST;
+            const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
+            const bool next_b = j + 1 < n_b;
+            if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
+            if (j < n_a) {
+              if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+              pf_phase[0] ^= 1u;
+              tc_fence_after();
+              pv(0, st, j > 0);
+              if (j + 1 < n_a) {
+                qk(0, st_n);
+                umma_commit(&s_full[0]);
+                if (j + 2 == n_a) umma_commit(&q_empty[0]);
+              } else {
                 umma_commit(&o_done[0]);
               }
-              if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-              pf_phase[1] ^= 1u;
-              tc_fence_after();
-              pv(1, st, j > 0);
-              umma_commit(&o_done[1]);
-              umma_commit(&v_empty[st]);
             }
-            kv = kv0 + n_b;
-          }
-        } else {
-          int kv = 0;
-          uint32_t pf_phase[2] = {0u, 0u};
-          bool ok = true;
-          for (int k = 0; ok; ++k) {
-            const int item = item_of(k);
-            if (item >= p.num_items) break;
-            const Item it = decode_item<CAUSAL>(item, p);
-            const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
-            const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);  // n_b >= n_a
-            if (!mbar_wait(&q_full[0], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-            if (!mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-            const int kv0 = kv;
-            // prologue: S_A(0), S_B(0)
-            {
-              const int st = kv0 % ST;
-              if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-              tc_fence_after();
-              qk(0, st);
-              umma_commit(&s_full[0]);
-              if (n_a == 1) umma_commit(&q_empty[0]);
-              qk(1, st);
+            if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            pf_phase[1] ^= 1u;
+            tc_fence_after();
+            pv(1, st, j > 0);
+            release(v_empty, st);
+            if (next_b) {
+              qk(1, st_n);
               umma_commit(&s_full[1]);
-              if (n_b == 1) umma_commit(&q_empty[1]);
-              umma_commit(&k_empty[st]);
+              release(k_empty, st_n);
+              if (j + 2 == n_b) umma_commit(&q_empty[1]);
+            } else {
+              umma_commit(&o_done[1]);
             }
-            for (int j = 0; j < n_b; ++j) {
-              const int st = (kv0 + j) % ST;
-              const uint32_t ph = ((kv0 + j) / ST) & 1;
-              const int st_n = (kv0 + j + 1) % ST;
-              const uint32_t ph_n = ((kv0 + j + 1) / ST) & 1;
-              const bool next_b = j + 1 < n_b;
-              if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-              if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-              if (j < n_a) {
-                if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-                pf_phase[0] ^= 1u;
-                tc_fence_after();
-                pv(0, st, j > 0);
-                if (j + 1 < n_a) {
-                  qk(0, st_n);
-                  umma_commit(&s_full[0]);
-                  if (j + 2 == n_a) umma_commit(&q_empty[0]);
-                } else {
-                  umma_commit(&o_done[0]);
-                }
-              }
-              if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-              pf_phase[1] ^= 1u;
-              tc_fence_after();
-              pv(1, st, j > 0);
-              umma_commit(&v_empty[st]);
-              if (next_b) {
-                qk(1, st_n);
-                umma_commit(&s_full[1]);
-                umma_commit(&k_empty[st_n]);
-                if (j + 2 == n_b) umma_commit(&q_empty[1]);
-              } else {
-                umma_commit(&o_done[1]);
-              }
-            }
-            kv = kv0 + n_b;
           }
+          kv = kv0 + n_b;
         }
-        umma_commit(drain);
-        mbar_wait(drain, 0, p.status, kDevTimeoutSoftmax, nullptr);
+        umma_commit(&drain[0]);
+        mbar_wait(&drain[0], 0, p.status, kDevTimeoutSoftmax, nullptr);
       }
     }
   } else {
