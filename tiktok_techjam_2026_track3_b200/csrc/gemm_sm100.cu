@@ -686,9 +686,11 @@ int dispatch_bn(const GemmArgs& g, cudaStream_t stream) {
   // More than one 128-row block: CTA pairs with 256 x 256 (or 256 x 128) tiles.
   // Otherwise one CTA per 128 x BN tile.  BN = 256 halves the A re-reads; 128
   // when N is small or would leave a half-empty tile column.
+  // 256 x 256 pairs keep 5 stages (160 KB) in flight: measured 3-5% faster
+  // than 4 on the layer's projections, whose operands stream from L2.
   const bool wide = g.n % 256 == 0 && g.n >= 512;
   if (g.m > kBM) {
-    if (wide) return launch_pair<TIn, TOut, 256, 4, EPI>(g, stream);
+    if (wide) return launch_pair<TIn, TOut, 256, 5, EPI>(g, stream);
     return launch_pair<TIn, TOut, 128, 5, EPI>(g, stream);
   }
   if (wide) return launch_one<TIn, TOut, 256, 3, EPI>(g, stream);
