@@ -18,6 +18,12 @@ the same metric through the public module call with the input copied in from
 pinned host memory and the output copied back inside the timed region.
 `--impl reference` times the reference algorithm on the host CPU (the fp32
 restatement in oracle/), the arm the driver compares against.
+
+`--block` (one GPU, fp16/bf16 configs) times instead one whole pre-norm
+transformer block (BaselineTransformerBlock: LayerNorm, attention layer,
+LayerNorm, GELU FFN with ffn_dim = --ffn-mult x D) through
+ttj_transformer_block_fwd, beside the same block in PyTorch eager ops on the
+same GPU (cuBLAS GEMMs, ATen LayerNorm / GELU, SDPA attention) for context.
 """
 
 from __future__ import annotations
@@ -53,6 +59,9 @@ def parse_args():
     ap.add_argument("--cpu-sample-seconds", type=float, default=15.0)
     ap.add_argument("--spinup-seconds", type=float, default=0.5,
                     help="untimed work after warm-up so clocks leave idle (0 under a profiler)")
+    ap.add_argument("--block", action="store_true",
+                    help="time one whole transformer block instead of the attention layer")
+    ap.add_argument("--ffn-mult", type=int, default=4, help="ffn_dim = ffn_mult * d_model (--block)")
     return ap.parse_args()
 
 
@@ -543,6 +552,102 @@ def run_ours(args, cfg):
     return 0
 
 
+def run_block(args, cfg):
+    """One transformer block per step through ttj_transformer_block_fwd (see the
+    module docstring), with the PyTorch eager block timed beside it."""
+    import ctypes as C
+    import torch.nn.functional as F
+    from tiktok_techjam_2026_track3_b200 import _lib, ops
+
+    if args.gpus != 1 or cfg.quant is not None:
+        raise SystemExit("--block runs on one GPU with a 16-bit config")
+    dev = torch.device("cuda", 0)
+    dtype = cfg.torch_dtype
+    B, S, D, H = cfg.batch, cfg.seq_len, cfg.d_model, cfg.num_heads
+    Fd = args.ffn_mult * D
+    T = B * S
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+
+    def rnd(*shape, scale=0.02, offset=0.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale + offset).to(dtype)
+
+    prm = {"ln1_w": rnd(D, offset=1.0), "ln1_b": rnd(D), "w_qkv": rnd(3 * D, D), "b_qkv": rnd(3 * D),
+           "w_o": rnd(D, D), "b_o": rnd(D), "ln2_w": rnd(D, offset=1.0), "ln2_b": rnd(D),
+           "w_in": rnd(Fd, D), "b_in": rnd(Fd), "w_out": rnd(D, Fd), "b_out": rnd(D)}
+    x = rnd(B, S, D, scale=1.0)
+    out = torch.empty_like(x)
+    lib = _lib.load()
+    dt = 0 if dtype == torch.float16 else 1
+    ws = torch.empty(lib.ttj_block_workspace_size(B, S, D, Fd, dt), dtype=torch.uint8, device=dev)
+    status = ops.status_word(dev)
+    stream = torch.cuda.current_stream(dev)
+    a = _lib.BlockArgs(x=x.data_ptr(), valid_token_mask=None, out=out.data_ptr(),
+                       workspace=ws.data_ptr(), workspace_bytes=ws.numel(), status=status.data_ptr(),
+                       batch=B, seq_len=S, d_model=D, num_heads=H, ffn_dim=Fd, eps1=1e-5, eps2=1e-5,
+                       causal=int(cfg.causal), dtype=dt, **{k: v.data_ptr() for k, v in prm.items()})
+
+    def ours():
+        rc = lib.ttj_transformer_block_fwd(C.byref(a), stream.cuda_stream)
+        if rc:
+            raise RuntimeError(lib.ttj_last_error().decode())
+
+    def torch_eager():
+        h = F.layer_norm(x, (D,), prm["ln1_w"], prm["ln1_b"], 1e-5)
+        q, k, v = F.linear(h, prm["w_qkv"], prm["b_qkv"]).view(B, S, 3, H, D // H).permute(2, 0, 3, 1, 4)
+        c = F.scaled_dot_product_attention(q, k, v, is_causal=cfg.causal).transpose(1, 2).reshape(B, S, D)
+        x1 = x + F.linear(c, prm["w_o"], prm["b_o"])
+        h2 = F.layer_norm(x1, (D,), prm["ln2_w"], prm["ln2_b"], 1e-5)
+        return x1 + F.linear(F.gelu(F.linear(h2, prm["w_in"], prm["b_in"])), prm["w_out"], prm["b_out"])
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def time_it(fn):
+        with torch.inference_mode():
+            for _ in range(args.warmup):
+                fn()
+            t_spin = time.perf_counter()
+            while time.perf_counter() - t_spin < args.spinup_seconds:
+                fn()
+                torch.cuda.synchronize(dev)
+            ms = []
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                ms.append(e0.elapsed_time(e1))
+        return sum(ms) / len(ms)
+
+    with ClockSampler(dev) as clk:
+        ours_ms = time_it(ours)
+    torch_ms = time_it(torch_eager)
+    ops.check_device_status(dev)
+    with torch.inference_mode():
+        err = float((out.float() - torch_eager().float()).abs().max())
+    from tiktok_techjam_2026_track3_b200.config import attention_flops
+    flops = attention_flops(cfg) + 2.0 * 2 * T * D * Fd
+    line = {
+        "metric": "transformer-block forward tokens/sec", "value": T / (ours_ms / 1e3), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ours_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {"float16": "fp16", "bfloat16": "bf16"}[cfg.dtype],
+        "data": "synthetic (seeded; x ~ N(0,1), weights ~ N(0,0.02), norm weights ~ 1 + N(0,0.02))",
+        "config": {"workload": f"block_{cfg.name}_ffn{Fd}", "batch": B, "seq_len": S, "d_model": D,
+                   "heads": H, "ffn_dim": Fd, "causal": cfg.causal,
+                   "l2": "flushed between timed steps (256 MB write, outside the events)"},
+        "block_tflops": flops / (ours_ms / 1e3) / 1e12,
+        "gpu_launches": 7 * args.steps,
+        "torch_eager": {"ms_per_step": torch_ms, "value": T / (torch_ms / 1e3),
+                        "max_abs_diff_vs_ours": err},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     from tiktok_techjam_2026_track3_b200.config import PRESETS
@@ -553,6 +658,8 @@ def main():
         cfg = cfg.with_(seq_len=args.seq)
     if args.impl == "reference":
         return run_reference(args, cfg)
+    if args.block:
+        return run_block(args, cfg)
     return run_ours(args, cfg)
 
 

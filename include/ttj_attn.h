@@ -11,6 +11,7 @@
  * Reference interfaces replaced (file:line in yyan115/Tiktok_TechJam_2026_Track3):
  *   torch_transformer_benchmark.py:85-122  BaselineSelfAttention.forward
  *   torch_transformer_benchmark.py:140     block residual  x + attention(...)
+ *   torch_transformer_benchmark.py:125-172 BaselineTransformerBlock / final norm
  *   Project/kernels/k008_int8_gemm.py:148-185  W8A8 recipe (_quant_rows,
  *                                           _int8_pack, _int8_linear)
  *
@@ -245,6 +246,69 @@ size_t ttj_int8_attn_layer_workspace_size(int64_t batch, int64_t seq_len, int64_
  * with fused dequant + bias + mask + residual.
  */
 int ttj_int8_attn_layer_fwd(const ttj_int8_attn_layer_args* args, ttj_stream_t stream);
+
+/* ------------------------------------------------------- transformer block */
+
+/*
+ * y[r,:] = (x[r,:] - mean) / sqrt(var + eps) * gamma + beta over rows of length
+ * d (biased variance, fp32 arithmetic), i.e. nn.LayerNorm(d, eps) of
+ * torch_transformer_benchmark.py:128-130 (norm1, norm2) and :159 (final_norm).
+ * Rows with row_mask[r] == 0 are written as zeros (the model's final
+ * masked_fill, :170-171); row_mask may be NULL.  gamma/beta are [d] in the same
+ * dtype as x.  Requires d % 8 == 0 and d <= 8192.
+ */
+int ttj_layernorm_fwd(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask,
+                      void* y, int64_t rows, int64_t d, float eps, int dtype, ttj_stream_t stream);
+
+/*
+ * y[M,N] = gelu(x[M,K] . w[N,K]^T + bias[N]) with the exact (erf) GELU:
+ * the block's F.gelu(self.ffn_in(...), approximate="none")
+ * (torch_transformer_benchmark.py:141) as one GEMM with a fused epilogue.
+ * Requires N % 32 == 0 and K % 8 == 0.
+ */
+int ttj_linear_gelu_fwd(const void* x, const void* w, const void* bias, void* y, int64_t m,
+                        int64_t n, int64_t k, int dtype, int* status, ttj_stream_t stream);
+
+/* Arguments of one pre-norm transformer block (BaselineTransformerBlock). */
+typedef struct ttj_block_args {
+  const void* x;                   /* [B,S,D] block input */
+  const void* ln1_w;               /* [D] norm1.weight */
+  const void* ln1_b;               /* [D] norm1.bias */
+  const void* w_qkv;               /* [3D,D] packed q/k/v_proj weights (as ttj_attn_layer_args) */
+  const void* b_qkv;               /* [3D] */
+  const void* w_o;                 /* [D,D] attention.out_proj.weight */
+  const void* b_o;                 /* [D] */
+  const void* ln2_w;               /* [D] norm2.weight */
+  const void* ln2_b;               /* [D] norm2.bias */
+  const void* w_in;                /* [F,D] ffn_in.weight */
+  const void* b_in;                /* [F] */
+  const void* w_out;               /* [D,F] ffn_out.weight */
+  const void* b_out;               /* [D] */
+  const uint8_t* valid_token_mask; /* [B,S] or NULL */
+  void* out;                       /* [B,S,D], must not alias x */
+  void* workspace;                 /* >= ttj_block_workspace_size() bytes */
+  size_t workspace_bytes;
+  int* status;                     /* device status word or NULL */
+  int64_t batch, seq_len, d_model, num_heads, ffn_dim;
+  float eps1, eps2;                /* norm1.eps, norm2.eps */
+  int causal;
+  int dtype;                       /* enum ttj_dtype */
+} ttj_block_args;
+
+/* Bytes of device workspace one block needs. */
+size_t ttj_block_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model, int64_t ffn_dim,
+                                int dtype);
+
+/*
+ * One BaselineTransformerBlock.forward (torch_transformer_benchmark.py:134-145):
+ *   x1  = x + mask(attention(norm1(x)))            (LayerNorm kernel + the layer's three)
+ *   out = mask_rows(x1 + ffn_out(gelu(ffn_in(norm2(x1)))))
+ * as six kernels: LayerNorm, QKV GEMM, flash attention, out-proj GEMM with
+ * bias+mask+residual, LayerNorm, ffn_in GEMM with bias+GELU, ffn_out GEMM with
+ * bias+residual and the block's final row zeroing (masked_fill, :143-144).
+ * Requires ffn_dim % 32 == 0 plus the attention layer's shape rules.
+ */
+int ttj_transformer_block_fwd(const ttj_block_args* args, ttj_stream_t stream);
 
 #ifdef __cplusplus
 }

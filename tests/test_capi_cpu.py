@@ -39,7 +39,8 @@ def test_version_and_status_strings():
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
 @pytest.mark.parametrize("cname,pyname", [("ttj_attn_layer_args", "AttnLayerArgs"),
-                                          ("ttj_int8_attn_layer_args", "Int8AttnLayerArgs")])
+                                          ("ttj_int8_attn_layer_args", "Int8AttnLayerArgs"),
+                                          ("ttj_block_args", "BlockArgs")])
 def test_struct_layout_matches_header(tmp_path, cname, pyname):
     """Every field offset of the ctypes mirror equals the C compiler's."""
     cls = getattr(_lib, pyname)
@@ -88,6 +89,23 @@ def test_argument_validation_without_device():
     assert lib.ttj_attn_layer_fwd(C.byref(a), None) == -1
     # int8 gemm needs K % 16
     assert lib.ttj_int8_gemm_s32(fake, fake, fake, 16, 32, 24, None, None) == -2
+    # LayerNorm: d must be a multiple of 8 and at most 8192
+    assert lib.ttj_layernorm_fwd(fake, fake, fake, None, fake, 4, 12, 1e-5, 0, None) == -2
+    assert lib.ttj_layernorm_fwd(fake, fake, fake, None, fake, 4, 16384, 1e-5, 0, None) == -2
+    assert lib.ttj_layernorm_fwd(None, fake, fake, None, fake, 4, 64, 1e-5, 0, None) == -1
+    assert lib.ttj_linear_gelu_fwd(fake, fake, fake, fake, 4, 40, 8, 0, None, None) == -2
+    # block: ffn_dim must be a multiple of 32, workspace must be large enough
+    b = _lib.BlockArgs(**{f: fake for f in ("x", "ln1_w", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o",
+                                            "ln2_w", "ln2_b", "w_in", "b_in", "w_out", "b_out")},
+                       out=fake * 2, workspace=fake, workspace_bytes=1 << 40, batch=1, seq_len=8,
+                       d_model=128, num_heads=2, ffn_dim=100, eps1=1e-5, eps2=1e-5, causal=1, dtype=0)
+    assert lib.ttj_transformer_block_fwd(C.byref(b), None) == -2
+    b.ffn_dim = 512
+    b.workspace_bytes = 64
+    assert lib.ttj_transformer_block_fwd(C.byref(b), None) == -6
+    b.workspace_bytes = 1 << 40
+    b.out = b.x
+    assert lib.ttj_transformer_block_fwd(C.byref(b), None) == -1
 
 
 def test_workspace_sizes():
@@ -96,6 +114,9 @@ def test_workspace_sizes():
     assert lib.ttj_attn_layer_workspace_size(8, 2048, 1024, 0) == t * 3 * d * 2 + t * d * 2
     assert lib.ttj_attn_layer_workspace_size(0, 2048, 1024, 0) == 0
     assert lib.ttj_int8_attn_layer_workspace_size(1, 128, 256, 1) >= 128 * 256 * (1 + 6 + 2)
+    # block: norm output, max(3D, F) wide buffer, context, x1
+    assert lib.ttj_block_workspace_size(8, 2048, 1024, 4096, 0) == t * d * 2 * 3 + t * 4096 * 2
+    assert lib.ttj_block_workspace_size(8, 2048, 1024, 1024, 0) == t * d * 2 * 3 + t * 3 * d * 2
 
 
 def test_missing_library_fails_loudly(tmp_path):

@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "ttj_attn_layer_workspace_size", "ttj_attn_layer_fwd", "ttj_attn_layer_fwd_noalloc",
     "ttj_int8_quant_rows", "ttj_int8_gemm_s32", "ttj_int8_linear_fwd",
     "ttj_int8_attn_layer_workspace_size", "ttj_int8_attn_layer_fwd",
+    "ttj_layernorm_fwd", "ttj_linear_gelu_fwd", "ttj_block_workspace_size", "ttj_transformer_block_fwd",
 )
 
 vp = C.c_void_p
@@ -60,6 +61,20 @@ class Int8AttnLayerArgs(C.Structure):
     ]
 
 
+class BlockArgs(C.Structure):
+    """Mirror of ``ttj_block_args``."""
+    _fields_ = [
+        ("x", vp), ("ln1_w", vp), ("ln1_b", vp), ("w_qkv", vp), ("b_qkv", vp),
+        ("w_o", vp), ("b_o", vp), ("ln2_w", vp), ("ln2_b", vp),
+        ("w_in", vp), ("b_in", vp), ("w_out", vp), ("b_out", vp),
+        ("valid_token_mask", vp), ("out", vp),
+        ("workspace", vp), ("workspace_bytes", C.c_size_t), ("status", vp),
+        ("batch", i64), ("seq_len", i64), ("d_model", i64), ("num_heads", i64), ("ffn_dim", i64),
+        ("eps1", C.c_float), ("eps2", C.c_float),
+        ("causal", ci), ("dtype", ci),
+    ]
+
+
 _SIGNATURES = {
     "ttj_version": (ci, []),
     "ttj_status_string": (C.c_char_p, [ci]),
@@ -79,6 +94,10 @@ _SIGNATURES = {
     "ttj_int8_linear_fwd": (ci, [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, ci, vp, vp]),
     "ttj_int8_attn_layer_workspace_size": (C.c_size_t, [i64, i64, i64, ci]),
     "ttj_int8_attn_layer_fwd": (ci, [C.POINTER(Int8AttnLayerArgs), vp]),
+    "ttj_layernorm_fwd": (ci, [vp, vp, vp, vp, vp, i64, i64, C.c_float, ci, vp]),
+    "ttj_linear_gelu_fwd": (ci, [vp, vp, vp, vp, i64, i64, i64, ci, vp, vp]),
+    "ttj_block_workspace_size": (C.c_size_t, [i64, i64, i64, i64, ci]),
+    "ttj_transformer_block_fwd": (ci, [C.POINTER(BlockArgs), vp]),
 }
 
 _lock = threading.Lock()

@@ -373,4 +373,114 @@ int ttj_int8_attn_layer_fwd(const ttj_int8_attn_layer_args* a, ttj_stream_t stre
                              a->out, T, D, D, a->dtype, a->status, stream);
 }
 
+int ttj_layernorm_fwd(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask,
+                      void* y, int64_t rows, int64_t d, float eps, int dtype, ttj_stream_t stream) {
+  if (int rc = check_dtype(dtype)) return rc;
+  TTJ_CHECK_ARG(x && gamma && beta && y, TTJ_ERR_INVALID_ARG, "x, gamma, beta and y must be non-NULL");
+  TTJ_CHECK_ARG(rows > 0 && d > 0, TTJ_ERR_INVALID_ARG, "rows and d must be positive");
+  TTJ_CHECK_ARG(eps >= 0.f, TTJ_ERR_INVALID_ARG, "eps must be non-negative");
+  TTJ_CHECK_ARG(d % 8 == 0 && d <= 8192, TTJ_ERR_UNSUPPORTED, "d must be a multiple of 8 and at most 8192");
+  TTJ_CHECK_ARG(aligned16(x) && aligned16(gamma) && aligned16(beta) && aligned16(y), TTJ_ERR_ALIGNMENT,
+                "x, gamma, beta and y must be 16-byte aligned");
+  return ttj::launch_layernorm(x, gamma, beta, row_mask, y, rows, d, eps, dtype, (cudaStream_t)stream);
+}
+
+int ttj_linear_gelu_fwd(const void* x, const void* w, const void* bias, void* y, int64_t m, int64_t n,
+                        int64_t k, int dtype, int* status, ttj_stream_t stream) {
+  if (int rc = check_dtype(dtype)) return rc;
+  TTJ_CHECK_ARG(x && w && bias && y, TTJ_ERR_INVALID_ARG, "x, w, bias and y must be non-NULL");
+  TTJ_CHECK_ARG(m > 0 && n > 0 && k > 0, TTJ_ERR_INVALID_ARG, "m, n, k must be positive");
+  TTJ_CHECK_ARG(n % 32 == 0, TTJ_ERR_UNSUPPORTED, "n must be a multiple of 32");
+  TTJ_CHECK_ARG(k % 8 == 0, TTJ_ERR_UNSUPPORTED, "k must be a multiple of 8");
+  TTJ_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), TTJ_ERR_UNSUPPORTED, "dimension too large");
+  TTJ_CHECK_ARG(aligned16(x) && aligned16(w) && aligned16(bias) && aligned16(y), TTJ_ERR_ALIGNMENT,
+                "x, w, bias and y must be 16-byte aligned");
+  ttj::GemmArgs g{};
+  g.a = x;
+  g.b = w;
+  g.bias = bias;
+  g.out = y;
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.in_dtype = dtype;
+  g.out_dtype = dtype;
+  g.epi = ttj::Epi::kBiasGelu;
+  g.status = status;
+  return ttj::launch_gemm(g, (cudaStream_t)stream);
+}
+
+size_t ttj_block_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model, int64_t ffn_dim,
+                                int dtype) {
+  (void)dtype;
+  if (batch <= 0 || seq_len <= 0 || d_model <= 0 || ffn_dim <= 0) return 0;
+  const size_t t = (size_t)batch * (size_t)seq_len, d = (size_t)d_model, f = (size_t)ffn_dim;
+  const size_t wide = 3 * d > f ? 3 * d : f;
+  return round_up(t * d * 2, 256)        /* normalised input (norm1, then norm2) */
+         + round_up(t * wide * 2, 256)   /* qkv, then the GELU activations */
+         + round_up(t * d * 2, 256)      /* attention context */
+         + round_up(t * d * 2, 256);     /* x1 = x + attention */
+}
+
+int ttj_transformer_block_fwd(const ttj_block_args* a, ttj_stream_t stream) {
+  TTJ_CHECK_ARG(a != nullptr, TTJ_ERR_INVALID_ARG, "args is NULL");
+  if (int rc = check_dtype(a->dtype)) return rc;
+  if (int rc = check_layer_shape(a->batch, a->seq_len, a->d_model, a->num_heads)) return rc;
+  TTJ_CHECK_ARG(a->ffn_dim > 0 && a->ffn_dim % 32 == 0 && a->ffn_dim < (1ll << 31), TTJ_ERR_UNSUPPORTED,
+                "ffn_dim must be a positive multiple of 32");
+  TTJ_CHECK_ARG(a->x && a->ln1_w && a->ln1_b && a->w_qkv && a->b_qkv && a->w_o && a->b_o && a->ln2_w &&
+                    a->ln2_b && a->w_in && a->b_in && a->w_out && a->b_out && a->out,
+                TTJ_ERR_INVALID_ARG, "x, parameters and out must be non-NULL");
+  TTJ_CHECK_ARG(a->out != a->x, TTJ_ERR_INVALID_ARG, "out must not alias x");
+  TTJ_CHECK_ARG(aligned16(a->x) && aligned16(a->ln1_w) && aligned16(a->ln1_b) && aligned16(a->w_qkv) &&
+                    aligned16(a->b_qkv) && aligned16(a->w_o) && aligned16(a->b_o) && aligned16(a->ln2_w) &&
+                    aligned16(a->ln2_b) && aligned16(a->w_in) && aligned16(a->b_in) && aligned16(a->w_out) &&
+                    aligned16(a->b_out) && aligned16(a->out),
+                TTJ_ERR_ALIGNMENT, "x, parameters and out must be 16-byte aligned");
+  const size_t need = ttj_block_workspace_size(a->batch, a->seq_len, a->d_model, a->ffn_dim, a->dtype);
+  TTJ_CHECK_ARG(a->workspace != nullptr && a->workspace_bytes >= need, TTJ_ERR_WORKSPACE,
+                "workspace missing or smaller than ttj_block_workspace_size()");
+  TTJ_CHECK_ARG(aligned16(a->workspace), TTJ_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  const int64_t T = a->batch * a->seq_len, D = a->d_model, F = a->ffn_dim;
+  const size_t wide = (size_t)(3 * D > F ? 3 * D : F);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  void* h = ws;                                   // norm1(x), later norm2(x1)
+  ws += round_up((size_t)T * D * 2, 256);
+  void* big = ws;                                 // qkv, later gelu(ffn_in(.))
+  ws += round_up((size_t)T * wide * 2, 256);
+  void* ctx = ws;
+  ws += round_up((size_t)T * D * 2, 256);
+  void* x1 = ws;
+  const uint8_t* mask = a->valid_token_mask;
+  int rc = ttj_layernorm_fwd(a->x, a->ln1_w, a->ln1_b, nullptr, h, T, D, a->eps1, a->dtype, stream);
+  if (rc) return rc;
+  rc = ttj_qkv_proj_fwd(h, a->w_qkv, a->b_qkv, big, T, D, a->dtype, a->status, stream);
+  if (rc) return rc;
+  rc = ttj_flash_attn_fwd(big, mask, ctx, a->batch, a->seq_len, a->num_heads, D / a->num_heads, a->causal,
+                          a->dtype, a->status, stream);
+  if (rc) return rc;
+  rc = ttj_linear_fwd(ctx, a->w_o, a->b_o, a->x, mask, x1, T, D, D, a->dtype, a->status, stream);
+  if (rc) return rc;
+  rc = ttj_layernorm_fwd(x1, a->ln2_w, a->ln2_b, nullptr, h, T, D, a->eps2, a->dtype, stream);
+  if (rc) return rc;
+  rc = ttj_linear_gelu_fwd(h, a->w_in, a->b_in, big, T, F, D, a->dtype, a->status, stream);
+  if (rc) return rc;
+  // out = mask_rows(x1 + ffn_out(.)): rows of invalid tokens become zero
+  ttj::GemmArgs g{};
+  g.a = big;
+  g.b = a->w_out;
+  g.bias = a->b_out;
+  g.residual = x1;
+  g.row_mask = mask;
+  g.out = a->out;
+  g.m = T;
+  g.n = D;
+  g.k = F;
+  g.in_dtype = a->dtype;
+  g.out_dtype = a->dtype;
+  g.epi = ttj::Epi::kBiasResidualZeroRows;
+  g.status = a->status;
+  return ttj::launch_gemm(g, (cudaStream_t)stream);
+}
+
 }  // extern "C"

@@ -127,7 +127,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
     }
     return;
   } else {
-    constexpr bool kResidual = EPI == (int)Epi::kBiasResidual || EPI == (int)Epi::kDequantResidual;
+    constexpr bool kZeroRows = EPI == (int)Epi::kBiasResidualZeroRows;
+    constexpr bool kGelu = EPI == (int)Epi::kBiasGelu;
+    constexpr bool kResidual =
+        EPI == (int)Epi::kBiasResidual || EPI == (int)Epi::kDequantResidual || kZeroRows;
     constexpr bool kDequant = EPI == (int)Epi::kDequant || EPI == (int)Epi::kDequantResidual;
     constexpr int kChunks = BN / kEpiBoxCols / 2;
     float row_scale = 0.f;
@@ -192,7 +195,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           float res[8];
           unpack8<TOut>(*slot, res);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = row_keep ? res[i] + v[i] : res[i];
+          for (int i = 0; i < 8; ++i) v[i] = row_keep ? res[i] + v[i] : (kZeroRows ? 0.f : res[i]);
+        } else if constexpr (kGelu) {
+          // Exact (erf) GELU of the biased product, as F.gelu(approximate="none")
+          // (torch_transformer_benchmark.py:141): x * 0.5 * (1 + erf(x / sqrt 2)).
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = v[i] * 0.5f * (1.f + erff(v[i] * 0.70710678118654752f));
         } else {
           // Output-row masking without a residual (the reference's masked_fill
           // of the attention output, torch_transformer_benchmark.py:120-121).
@@ -702,6 +710,9 @@ int dispatch_epi(const GemmArgs& g, cudaStream_t stream) {
   switch (g.epi) {
     case Epi::kBias: return dispatch_bn<TIn, TOut, (int)Epi::kBias>(g, stream);
     case Epi::kBiasResidual: return dispatch_bn<TIn, TOut, (int)Epi::kBiasResidual>(g, stream);
+    case Epi::kBiasGelu: return dispatch_bn<TIn, TOut, (int)Epi::kBiasGelu>(g, stream);
+    case Epi::kBiasResidualZeroRows:
+      return dispatch_bn<TIn, TOut, (int)Epi::kBiasResidualZeroRows>(g, stream);
     default: return fail(TTJ_ERR_INVALID_ARG, "epilogue not valid for 16-bit operands");
   }
 }

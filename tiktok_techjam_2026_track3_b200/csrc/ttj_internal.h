@@ -46,6 +46,8 @@ enum class Epi : int {
   kRawS32 = 2,          // y = acc (int32)
   kDequant = 3,         // y = acc * (s_a * s_w) + bias
   kDequantResidual = 4, // y = residual + mask(acc * (s_a * s_w) + bias)
+  kBiasGelu = 5,        // y = gelu_erf(acc + bias)
+  kBiasResidualZeroRows = 6, // y = mask(residual + acc + bias): masked rows become 0
 };
 
 struct GemmArgs {
@@ -78,6 +80,11 @@ struct AttnArgs {
 int launch_flash_attn(const AttnArgs& a, cudaStream_t stream);
 
 int launch_wait_timeout_selftest(int* status, int64_t limit_us, cudaStream_t stream);
+
+// LayerNorm over rows of length d (d % 8 == 0, d <= 8192); rows with a zero
+// row_mask byte are written as zeros.
+int launch_layernorm(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask,
+                     void* y, int64_t rows, int64_t d, float eps, int dtype, cudaStream_t stream);
 
 int launch_quant_rows(const void* x, int8_t* q, float* scale, int64_t rows, int64_t cols,
                       int dtype, cudaStream_t stream);

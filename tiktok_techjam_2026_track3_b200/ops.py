@@ -200,6 +200,87 @@ def attn_layer(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, w_o: t
     return out
 
 
+# ------------------------------------------------------- transformer block
+
+def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
+              row_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """nn.LayerNorm over the last dimension (fp32 arithmetic); rows whose mask
+    entry is False come out as zeros."""
+    lib = _lib.load()
+    x = _cuda(x, "x")
+    dt = _dtype_code(x)
+    d = x.shape[-1]
+    rows = x.numel() // d
+    if weight.dtype != x.dtype or bias.dtype != x.dtype:
+        raise RuntimeError("weight and bias must share x's dtype")
+    rm = None
+    if row_mask is not None:
+        rm = _cuda(row_mask.reshape(-1), "row_mask")
+        if rm.numel() != rows:
+            raise RuntimeError("row_mask must have one entry per row")
+        rm = rm.view(torch.uint8) if rm.dtype == torch.bool else (rm != 0).view(torch.uint8)
+    y = torch.empty_like(x)
+    rc = lib.ttj_layernorm_fwd(x.data_ptr(), _cuda(weight, "weight").data_ptr(),
+                               _cuda(bias, "bias").data_ptr(), _ptr(rm), y.data_ptr(), rows, d,
+                               float(eps), dt, _stream(x.device))
+    _lib.check(rc, "ttj_layernorm_fwd")
+    return y
+
+
+def linear_gelu(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """gelu(x w^T + b) with the exact (erf) GELU, one GEMM launch."""
+    lib = _lib.load()
+    x, w, bias = _cuda(x, "x"), _cuda(w, "w"), _cuda(bias, "bias")
+    dt = _dtype_code(x)
+    if w.dtype != x.dtype or bias.dtype != x.dtype:
+        raise RuntimeError("x, w and bias must share one dtype")
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w.shape[0]
+    y = torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
+    rc = lib.ttj_linear_gelu_fwd(x.data_ptr(), w.data_ptr(), bias.data_ptr(), y.data_ptr(), m, n, k, dt,
+                                 status_word(x.device).data_ptr(), _stream(x.device))
+    _lib.check(rc, "ttj_linear_gelu_fwd")
+    return y
+
+
+BLOCK_PARAMS = ("ln1_w", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_w", "ln2_b",
+                "w_in", "b_in", "w_out", "b_out")
+
+
+def transformer_block(x: torch.Tensor, params: Dict[str, torch.Tensor], num_heads: int,
+                      causal: bool, eps1: float, eps2: float,
+                      valid_token_mask: Optional[torch.Tensor] = None,
+                      out: Optional[torch.Tensor] = None,
+                      workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One pre-norm block (BaselineTransformerBlock.forward) in six launches;
+    ``params`` holds the tensors named in BLOCK_PARAMS (w_qkv packed q|k|v)."""
+    lib = _lib.load()
+    x = _cuda(x, "x")
+    dt = _dtype_code(x)
+    B, S, D = x.shape
+    ptrs = {}
+    for name in BLOCK_PARAMS:
+        t = params[name]
+        if t.dtype != x.dtype or t.device != x.device:
+            raise RuntimeError(f"{name} must be {x.dtype} on {x.device}")
+        ptrs[name] = _cuda(t, name).data_ptr()
+    F = params["w_in"].shape[0]
+    km = _mask_u8(valid_token_mask, B, S)
+    if out is None:
+        out = torch.empty_like(x)
+    need = lib.ttj_block_workspace_size(B, S, D, F, dt)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    a = _lib.BlockArgs(x=x.data_ptr(), valid_token_mask=_ptr(km), out=out.data_ptr(),
+                       workspace=workspace.data_ptr(), workspace_bytes=workspace.numel(),
+                       status=status_word(x.device).data_ptr(), batch=B, seq_len=S, d_model=D,
+                       num_heads=num_heads, ffn_dim=F, eps1=float(eps1), eps2=float(eps2),
+                       causal=int(bool(causal)), dtype=dt, **ptrs)
+    _lib.check(lib.ttj_transformer_block_fwd(C.byref(a), _stream(x.device)), "ttj_transformer_block_fwd")
+    return out
+
+
 # ---------------------------------------------------------------------- int8
 
 def int8_quant_rows(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
