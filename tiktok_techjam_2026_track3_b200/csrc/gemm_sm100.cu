@@ -38,7 +38,12 @@ constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kEpiBoxRows = 32;
 constexpr int kEpiBoxCols = 64;                       // 16-bit: one 128-byte swizzle row
 constexpr int kEpiBoxBytes = kEpiBoxRows * 128;       // 4 KB
-constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBoxBytes;  // two buffers per warp: 64 KB
+// Staging buffers per epilogue warp.  One (32 KB in all) leaves room for a
+// deeper operand ring (measured: 6 stages + 1 buffer beat 5 stages + 2 buffers
+// by 2% on the layer's projections; the epilogue overlaps the next tile's MMAs
+// and has slack for the serialisation).
+constexpr int kEpiBufs = 1;
+constexpr int kEpiBytes = kEpiWarps * kEpiBufs * kEpiBoxBytes;
 constexpr int kBarrierBytes = 512;
 
 struct GemmParams {
@@ -64,7 +69,7 @@ struct GemmLayout {
 
 // Per-warp epilogue state kept across tiles (scalars, so it stays in registers).
 struct EpiState {
-  uint8_t* buf0;       // two 1024-aligned 4 KB staging buffers
+  uint8_t* buf0;       // kEpiBufs 1024-aligned 4 KB staging buffers (buf1 == buf0 if one)
   uint8_t* buf1;
   uint64_t* bar0;      // residual-load barriers, one per buffer
   uint64_t* bar1;
@@ -142,11 +147,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       const int c = col_half * kChunks + cc;
       const int n0 = n_blk * BN + c * kEpiBoxCols;
       const int b = es.next;
-      es.next ^= 1;
+      if (kEpiBufs == 2) es.next ^= 1;
       uint8_t* buf = b ? es.buf1 : es.buf0;
       uint64_t* bar = b ? es.bar1 : es.bar0;
-      // The store issued from this buffer two chunks ago must have read it.
-      if (lane == 0) bulk_wait_group_read<1>();
+      // The store issued from this buffer kEpiBufs chunks ago must have read it.
+      if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();
       __syncwarp();
       if (n0 >= p.N) continue;  // whole chunk past the last column (uniform)
       if constexpr (kResidual) {
@@ -228,10 +233,10 @@ constexpr CUtensorMapDataType tmap_dtype() {
 
 template <typename TOut>
 __device__ __forceinline__ void init_epi_state(EpiState& es, uint8_t* epi_base, uint64_t* res_bars, int ew) {
-  es.buf0 = epi_base + (2 * ew) * kEpiBoxBytes;
-  es.buf1 = epi_base + (2 * ew + 1) * kEpiBoxBytes;
+  es.buf0 = epi_base + (kEpiBufs * ew) * kEpiBoxBytes;
+  es.buf1 = es.buf0 + (kEpiBufs - 1) * kEpiBoxBytes;
   es.bar0 = res_bars + 2 * ew;
-  es.bar1 = res_bars + 2 * ew + 1;
+  es.bar1 = es.bar0 + (kEpiBufs - 1);
   es.phase0 = es.phase1 = 0u;
   es.next = 0;
 }
@@ -694,15 +699,15 @@ int dispatch_bn(const GemmArgs& g, cudaStream_t stream) {
   // More than one 128-row block: CTA pairs with 256 x 256 (or 256 x 128) tiles.
   // Otherwise one CTA per 128 x BN tile.  BN = 256 halves the A re-reads; 128
   // when N is small or would leave a half-empty tile column.
-  // 256 x 256 pairs keep 5 stages (160 KB) in flight: measured 3-5% faster
-  // than 4 on the layer's projections, whose operands stream from L2.
+  // 256 x 256 pairs keep 6 stages (192 KB) in flight: the layer's projections
+  // stream their operands from L2 and measured faster with every added stage.
   const bool wide = g.n % 256 == 0 && g.n >= 512;
   if (g.m > kBM) {
-    if (wide) return launch_pair<TIn, TOut, 256, 5, EPI>(g, stream);
-    return launch_pair<TIn, TOut, 128, 5, EPI>(g, stream);
+    if (wide) return launch_pair<TIn, TOut, 256, 6, EPI>(g, stream);
+    return launch_pair<TIn, TOut, 128, 7, EPI>(g, stream);
   }
-  if (wide) return launch_one<TIn, TOut, 256, 3, EPI>(g, stream);
-  return launch_one<TIn, TOut, 128, 4, EPI>(g, stream);
+  if (wide) return launch_one<TIn, TOut, 256, 4, EPI>(g, stream);
+  return launch_one<TIn, TOut, 128, 6, EPI>(g, stream);
 }
 
 template <typename TIn, typename TOut>
