@@ -428,6 +428,7 @@ int ttj_transformer_block_fwd(const ttj_block_args* a, ttj_stream_t stream) {
   if (int rc = check_layer_shape(a->batch, a->seq_len, a->d_model, a->num_heads)) return rc;
   TTJ_CHECK_ARG(a->ffn_dim > 0 && a->ffn_dim % 32 == 0 && a->ffn_dim < (1ll << 31), TTJ_ERR_UNSUPPORTED,
                 "ffn_dim must be a positive multiple of 32");
+  TTJ_CHECK_ARG(a->batch * a->seq_len * a->ffn_dim < (1ll << 46), TTJ_ERR_UNSUPPORTED, "tensor too large");
   TTJ_CHECK_ARG(a->x && a->ln1_w && a->ln1_b && a->w_qkv && a->b_qkv && a->w_o && a->b_o && a->ln2_w &&
                     a->ln2_b && a->w_in && a->b_in && a->w_out && a->b_out && a->out,
                 TTJ_ERR_INVALID_ARG, "x, parameters and out must be non-NULL");

@@ -258,6 +258,8 @@ def transformer_block(x: torch.Tensor, params: Dict[str, torch.Tensor], num_head
     lib = _lib.load()
     x = _cuda(x, "x")
     dt = _dtype_code(x)
+    if x.dim() != 3:
+        raise RuntimeError(f"x must be [B,S,D], got {tuple(x.shape)}")
     B, S, D = x.shape
     ptrs = {}
     for name in BLOCK_PARAMS:
@@ -266,6 +268,8 @@ def transformer_block(x: torch.Tensor, params: Dict[str, torch.Tensor], num_head
             raise RuntimeError(f"{name} must be {x.dtype} on {x.device}")
         ptrs[name] = _cuda(t, name).data_ptr()
     F = params["w_in"].shape[0]
+    if params["w_in"].shape != (F, D) or params["w_out"].shape != (D, F) or params["w_qkv"].shape != (3 * D, D):
+        raise RuntimeError("block weights do not match d_model / ffn_dim")
     km = _mask_u8(valid_token_mask, B, S)
     if out is None:
         out = torch.empty_like(x)
