@@ -71,11 +71,20 @@ struct AttnSmem {
   static constexpr bool kSepP = HD == 64;           // separate P buffers in TMEM
   static constexpr int kStages = HD == 64 ? 4 : 2;
   static constexpr int kTileBytes = HD * 2 * 128;  // 128 rows x HD x 2 bytes
-  static constexpr int kQOff = 0;                   // Q_A, Q_B
-  static constexpr int kKOff = 2 * kTileBytes;
+  // Q tiles: head_dim 64 double-buffers them (the next item's Q arrives while
+  // this item runs); head_dim 128 has no room.
+  static constexpr int kQBufs = HD == 64 ? 2 : 1;
+  static constexpr int kQOff = 0;                   // [kQBufs][Q_A, Q_B]
+  static constexpr int kKOff = 2 * kQBufs * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  // head_dim 64: the context rows leave through a TMA store from a 4 KB
+  // staging box per softmax warp (32 rows x 128 bytes, 128-byte swizzle);
+  // measured: per-thread 16-byte row stores took 1-2.5K cycles per item end.
+  static constexpr bool kTmaEpi = HD == 64;
+  static constexpr int kEpiOff = kVOff + kStages * kTileBytes;
+  static constexpr int kBarOff = kEpiOff + (kTmaEpi ? 8 * 32 * 128 : 0);
   static constexpr int kTotal = 1024 + kBarOff + 512;
+  static_assert(kTotal <= 232448, "shared memory budget");
   // TMEM columns
   static constexpr uint32_t kColP = kSepP ? 256 : 0;      // + t*64 (separate) / + t*128 (over S)
   static constexpr uint32_t kColO = kSepP ? 384 : 256;    // + t*HD
@@ -146,7 +155,8 @@ __device__ __forceinline__ int kv_tiles(int pair, int t, int S) {
 
 template <typename T, int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
-flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
+flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_ctx,
+                 const AttnParams p) {
   using L = AttnSmem<HD>;
   constexpr int ST = L::kStages;
   constexpr bool kSepP = L::kSepP;
@@ -163,9 +173,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* q_full = bars;              // [2] per tile: Q_t loaded
-  uint64_t* q_empty = q_full + 2;       // [2] per tile: last Q_t K^T of the item done
-  uint64_t* k_full = q_empty + 2;       // [ST]
+  uint64_t* q_full = bars;              // [kQBufs][2] per tile: Q_t loaded
+  uint64_t* q_empty = q_full + 4;       // [kQBufs][2] per tile: last Q_t K^T of the item done
+  uint64_t* k_full = q_empty + 4;       // [ST]
   uint64_t* k_empty = k_full + ST;      // [2][ST] per tile: its Q_t K^T done with the stage
   uint64_t* v_full = k_empty + 2 * ST;  // [ST]
   uint64_t* v_empty = v_full + ST;      // [2][ST] per tile: its P_t V done with the stage
@@ -190,8 +200,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
       }
     }
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&q_full[t], 1);
-      mbar_init(&q_empty[t], 1);
+      for (int b = 0; b < L::kQBufs; ++b) {
+        mbar_init(&q_full[b * 2 + t], 1);
+        mbar_init(&q_empty[b * 2 + t], 1);
+      }
       mbar_init(&s_full[t], 1);
       mbar_init(&s_free[t], 128);
       mbar_init(&p_full[t], 128);
@@ -265,19 +277,21 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
         const Item it = decode_item<CAUSAL>(item, p);
         bool ok = true;
         for (int t = 0; t < 2 && ok; ++t) {
-          ok = mbar_wait(&q_empty[t], (k & 1) ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag);
+          const int qb = k % L::kQBufs;
+          const uint32_t qph = (k / L::kQBufs) & 1;
+          ok = mbar_wait(&q_empty[qb * 2 + t], qph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag);
           if (!ok) break;
-          mbar_arrive_expect_tx(&q_full[t], L::kTileBytes);
+          mbar_arrive_expect_tx(&q_full[qb * 2 + t], L::kTileBytes);
           for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sQ + t * L::kTileBytes + c * kChunkBytes, &tm, &q_full[t], it.h * HD + 64 * c,
+            tma_load_3d(sQ + (qb * 2 + t) * L::kTileBytes + c * kChunkBytes, &tm, &q_full[qb * 2 + t], it.h * HD + 64 * c,
                         it.pair * 2 * kBM + t * kBM, it.b);
         }
         if (!ok) break;
       }
     } else if (lane == 0 && (warp == 1 || (kSepP && warp == 3))) {
       // ------------------------------------------------------------ MMA issue
-      auto qk = [&](int t, int st) {
-        const uint32_t q_addr = smem_u32(sQ + t * L::kTileBytes);
+      auto qk = [&](int t, int st, int qb) {
+        const uint32_t q_addr = smem_u32(sQ + (qb * 2 + t) * L::kTileBytes);
         const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -318,7 +332,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
         uint32_t sfree_ph = 0u, pf_ph = 0u;
         auto issue_qk = [&]() -> bool {
           if (!qk_live) return true;
-          if (qk_j == 0 && !mbar_wait(&q_full[t], qk_k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) return false;
+          const int qb = qk_k % L::kQBufs;
+          if (qk_j == 0 && !mbar_wait(&q_full[qb * 2 + t], (qk_k / L::kQBufs) & 1, p.status, kDevTimeoutTmaFull,
+                                      abort_flag))
+            return false;
           if (!qk_first) {
             if (!mbar_wait(&s_free[t], sfree_ph, p.status, kDevTimeoutSoftmax, abort_flag)) return false;
             sfree_ph ^= 1u;
@@ -327,12 +344,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
           const int st = kvi % ST;
           if (!mbar_wait(&k_full[st], (kvi / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) return false;
           tc_fence_after();
-          qk(t, st);
+          qk(t, st, qb);
           umma_commit(&s_full[t]);
           umma_commit(&k_empty[t * ST + st]);
           qk_first = false;
           if (++qk_j == qk_n) {  // last S_t of the item: Q_t may be replaced
-            umma_commit(&q_empty[t]);
+            umma_commit(&q_empty[qb * 2 + t]);
             qk_kv0 += qk_nb;
             qk_j = 0;
             ++qk_k;
@@ -349,7 +366,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
           const int n = kv_tiles<CAUSAL>(it.pair, t, p.S);
           const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);
           for (int j = 0; j < n; ++j) {
-            if (!issue_qk()) { ok = false; break; }  // S_t(j+1) or the next item's S_t(0)
+            // S_t(j+1), or the next item's S_t(0) (its Q is double-buffered, so
+            // normally already loaded), then this key tile's P.V.  Issuing the
+            // item's last P.V first measured slower for causal items.
+            if (!issue_qk()) { ok = false; break; }
             if (!mbar_wait(&p_full[t], pf_ph, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
             pf_ph ^= 1u;
             const int kvi = kv0 + j;
@@ -367,6 +387,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
         umma_commit(&drain[t]);
         mbar_wait(&drain[t], 0, p.status, kDevTimeoutSoftmax, nullptr);
       } else {
+        static_assert(L::kQBufs == 1, "the single-issuer schedule uses one Q buffer per tile");
         // P over S: one thread issues both tiles, PV_A(j) QK_A(j+1) PV_B(j)
         // QK_B(j+1) (measured faster here than one thread per tile: each tile's
         // next S waits for its own P.V, and the fixed interleave keeps the two
@@ -390,10 +411,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
             const int st = kv0 % ST;
             if (!mbar_wait(&k_full[st], (kv0 / ST) & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
             tc_fence_after();
-            qk(0, st);
+            qk(0, st, 0);
             umma_commit(&s_full[0]);
             if (n_a == 1) umma_commit(&q_empty[0]);
-            qk(1, st);
+            qk(1, st, 0);
             umma_commit(&s_full[1]);
             if (n_b == 1) umma_commit(&q_empty[1]);
             release(k_empty, st);
@@ -412,7 +433,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
               tc_fence_after();
               pv(0, st, j > 0);
               if (j + 1 < n_a) {
-                qk(0, st_n);
+                qk(0, st_n, 0);
                 umma_commit(&s_full[0]);
                 if (j + 2 == n_a) umma_commit(&q_empty[0]);
               } else {
@@ -425,7 +446,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
             pv(1, st, j > 0);
             release(v_empty, st);
             if (next_b) {
-              qk(1, st_n);
+              qk(1, st_n, 0);
               umma_commit(&s_full[1]);
               release(k_empty, st_n);
               if (j + 2 == n_b) umma_commit(&q_empty[1]);
@@ -579,6 +600,34 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
       od_phase ^= 1u;
       tc_fence_after();
       const float inv_l = 1.f / l_run;
+      if constexpr (L::kTmaEpi) {
+        // this warp's 32 rows x 64 columns: swizzled staging box, one TMA store
+        uint8_t* box = smem + L::kEpiOff + (warp - 4) * (32 * 128);
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous item's store has read the box
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o + c * 32, o);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = Pack<T>::two(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
+            w.y = Pack<T>::two(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
+            w.z = Pack<T>::two(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
+            w.w = Pack<T>::two(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
+            const int chunk = c * 4 + q;  // 16-byte chunk of the 128-byte row
+            *reinterpret_cast<uint4*>(box + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = w;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tm_ctx, box, it.h * HD, q0 + lg * 32, it.b);  // rows >= S are clipped
+          bulk_commit_group();
+        }
+        continue;
+      }
       T* dst = static_cast<T*>(p.ctx) + ((int64_t)it.b * p.S + q_row) * p.D + it.h * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
@@ -600,6 +649,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
       // The next item's first P.V overwrites O_t only after this thread's next
       // p_full arrival, which follows these loads.
     }
+    if (L::kTmaEpi && lane == 0) bulk_wait_group_all();  // context stores complete before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -619,6 +669,16 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                        3, a.qkv, dims, strides, box);
   if (rc) return rc;
+  CUtensorMap tm_ctx = tm;  // unused unless L::kTmaEpi
+  if (L::kTmaEpi) {
+    const uint64_t cdims[3] = {(uint64_t)D, (uint64_t)a.seq_len, (uint64_t)a.batch};
+    const uint64_t cstrides[2] = {(uint64_t)(D * 2), (uint64_t)(a.seq_len * D * 2)};
+    const uint32_t cbox[3] = {64, 32, 1};
+    rc = encode_tmap(&tm_ctx, std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                     3, a.ctx, cdims, cstrides, cbox);
+    if (rc) return rc;
+  }
   AttnParams p;
   p.ctx = a.ctx;
   p.key_mask = a.key_mask;
@@ -643,7 +703,7 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   }
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
   const int grid = p.num_items < sm_count() ? p.num_items : sm_count();
-  kern<<<grid, kThreads, L::kTotal, stream>>>(tm, p);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(tm, tm_ctx, p);
   TTJ_CUDA_TRY(cudaGetLastError());
   return TTJ_OK;
 }
