@@ -51,7 +51,7 @@ L2_FLUSH_BYTES = 256 << 20
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
@@ -177,6 +177,20 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return {"bf16_tflops": d["bf16_tflops"], "hbm_gbs": d["hbm_gbs"], "source": "measured"}
     return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def exp_roofline(cfg, attn_ms: float, clocks):
+    """The attention's other ceiling: softmax exponentials (one per score the
+    reference evaluates: B*H*S^2, B*H*S(S+1)/2 when causal) against the
+    exponential unit's 16 results per clock per SM at the sampled SM clock."""
+    B, H, S = cfg.batch, cfg.num_heads, cfg.seq_len
+    exps = B * H * (S * (S + 1) / 2 if cfg.causal else S * S)
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    peak = 16.0 * sms * mhz * 1e6
+    achieved = exps / (attn_ms / 1e3)
+    return {"achieved": achieved, "peak": peak, "unit": "exp/s", "frac": achieved / peak,
+            "peak_basis": f"16 exp/clk/SM x {sms} SMs x {mhz:.0f} MHz (sampled SM clock)"}
 
 
 def ncu_traffic(kernel: str, workload: str):
@@ -559,7 +573,8 @@ def run_ours(args, cfg):
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak_tf,
                      "unit": "TFLOP/s", "frac": achieved / peak_tf,
                      "peak_source": f"{peaks['source']} ({'2x ' if cfg.quant else ''}bf16 dense burst)",
-                     "traffic": ncu_traffic(dom, cfg.name)},
+                     "traffic": ncu_traffic(dom, cfg.name),
+                     "exp_unit": exp_roofline(cfg, statistics.mean(attn_ms), clocks)},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nbytes,
                 "d2h_bytes_per_step": nbytes,
                 "mode": "B200AttentionLayer calls through HostPipeline (copies of steps i+1 / i-1 overlap step i)",
