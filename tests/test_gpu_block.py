@@ -57,6 +57,33 @@ def test_linear_gelu_matches_fp32(dt, m, n, k):
     assert rep.passed, str(rep)
 
 
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_gelu_epilogue_matches_exact_erf(dt):
+    """The GELU epilogue against exact GELU evaluated in float64 (through erfc,
+    so the negative tail is exact) on the same pre-activations: a one-hot x
+    makes every accumulator exactly one weight.  The epilogue's erfc (fractional
+    error < 1.2e-7) must give the correctly rounded 16-bit value almost
+    everywhere and be off by at most one unit in the last place anywhere --
+    closer than torch's own fp32 GELU, which loses the tail to cancellation in
+    1 + erf(z), as the last assertion records."""
+    dtype = DT[dt]
+    K, N, M = 64, 1024, 256
+    vals = torch.linspace(-12.0, 12.0, K * N).to(dtype)          # pre-activations, exact in dtype
+    w = vals.view(N, K)
+    x = torch.zeros(M, K, dtype=dtype)
+    x[torch.arange(M), torch.arange(M) % K] = 1.0                 # row m picks column m % K of w
+    b = torch.zeros(N, dtype=dtype)
+    out = ops.linear_gelu(x.cuda(), w.cuda(), b.cuda()).cpu().double()
+    pre = w.double().T[torch.arange(M) % K]                       # [M, N] exact pre-activations
+    exact = (0.5 * pre * torch.special.erfc(-pre / 2.0 ** 0.5)).to(dtype).double()
+    ulp = (exact.abs() * 2.0 ** (-10 if dt == "fp16" else -7)).clamp_min(2.0 ** -24)
+    diff = (out - exact).abs()
+    assert bool((diff <= ulp).all()), f"max diff {diff.max():.3g}"
+    assert float((diff == 0).double().mean()) > 0.99
+    torch_fp32 = F.gelu(pre.float(), approximate="none").to(dtype).double()
+    assert float((torch_fp32 - exact).abs().max()) <= 2e-3          # same tolerance as the layer
+
+
 def _block(D, H, Fdim, seed):
     torch.manual_seed(seed)
     blk = BaselineTransformerBlockRef(D, H, Fdim)
