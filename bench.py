@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
 
 Prints ONE JSON line on rank 0.  A step is one attention-layer forward over
-one batch of the workload (BASELINE config 2 by default: B8 S2048 D1024 H16,
+one batch of the workload (benchmark configuration 2 by default: B8 S2048 D1024 H16,
 causal, fp16).  Multi-GPU runs (torchrun, one process per GPU) are weak
 scaling: every rank runs its own batch of the workload, there is no
 collective on the data path, and `value` is the tokens of all ranks divided

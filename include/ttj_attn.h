@@ -217,7 +217,7 @@ int ttj_int8_linear_fwd(const int8_t* a, const float* s_a, const int8_t* w, cons
                         void* y, int64_t m, int64_t n, int64_t k, int out_dtype, int* status,
                         ttj_stream_t stream);
 
-/* Arguments of the int8-projection attention layer. */
+/* Arguments of the int8-projection attention layer (benchmark configuration 3). */
 typedef struct ttj_int8_attn_layer_args {
   const void* x;                   /* [B,S,D] fp16/bf16 */
   const int8_t* w_qkv;             /* [3D,D] int8, per-output-channel quantised */

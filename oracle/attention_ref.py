@@ -71,7 +71,7 @@ class LayerWeights:
 
 def make_weights(d_model: int, seed: int, std: float = 0.02,
                  dtype: torch.dtype = torch.float32) -> LayerWeights:
-    """Seeded N(0, std) weights and biases, the BASELINE configs' choice.
+    """Seeded N(0, std) weights and biases, the benchmark configurations' choice.
 
     The reference initialises with ``nn.Linear`` defaults; the benchmark then
     copies one state dict into both models (Ref:203-213), so any seeded values

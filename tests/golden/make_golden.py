@@ -44,7 +44,7 @@ def _load(path: Path, name: str):
 
 # (name, batch, seq, d_model, heads, causal, padding_ratio, seed)
 ATTENTION_CASES = [
-    ("cfg1_noncausal", 2, 128, 256, 4, False, 0.0, 1234),   # BASELINE config 1 shape
+    ("cfg1_noncausal", 2, 128, 256, 4, False, 0.0, 1234),   # benchmark configuration 1 shape
     ("cfg1_causal", 2, 128, 256, 4, True, 0.0, 1235),
     ("padded_causal", 3, 96, 128, 2, True, 0.4, 1236),       # prefix key-padding masks
     ("ragged_hd128", 1, 77, 256, 2, False, 0.3, 1237),       # S not a tile multiple, hd 128
@@ -55,7 +55,7 @@ ATTENTION_CASES = [
 def make_attention_fixture(ref, name, B, S, D, H, causal, padding, seed):
     torch.manual_seed(seed)
     layer = ref.BaselineSelfAttention(D, H)
-    # Seeded N(0, 0.02) weights (the BASELINE configs' init) loaded through the
+    # Seeded N(0, 0.02) weights (the benchmark configurations' init) loaded through the
     # same strict load_state_dict path the benchmark uses.
     g = torch.Generator().manual_seed(seed + 7)
     sd = {k: torch.randn(v.shape, generator=g) * 0.02 for k, v in layer.state_dict().items()}

@@ -1,4 +1,4 @@
-"""W8A8 attention layer (BASELINE config 3 recipe) against the integer oracle
+"""W8A8 attention layer (benchmark configuration 3 recipe) against the integer oracle
 of the same recipe (Project/kernels/k008_int8_gemm.py:148-185), stage by stage.
 
 Why stagewise: per-token int8 quantisation of the attention context turns

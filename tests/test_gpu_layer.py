@@ -2,7 +2,7 @@
 drop-in module, against the fp32 oracle on the same rounded inputs.
 
 Seeds follow the reference benchmark's policy: seeds 1234.. consecutive
-(torch_transformer_benchmark.py:382-388), seven of them for BASELINE config 2.
+(torch_transformer_benchmark.py:382-388), seven of them for benchmark configuration 2.
 """
 
 import pytest
@@ -50,7 +50,7 @@ def test_layer_on_golden_inputs(golden_dir, dt, name):
 
 @pytest.mark.parametrize("seed", range(1234, 1241))
 def test_config2_seven_seeds(seed):
-    """BASELINE config 2 at full size: B8 S2048 D1024 H16 causal fp16."""
+    """benchmark configuration 2 at full size: B8 S2048 D1024 H16 causal fp16."""
     B, S, D, H = 8, 2048, 1024, 16
     x, _ = generate_case(B, S, D, seed, dtype=torch.float16)
     w = make_weights(D, seed, dtype=torch.float16)

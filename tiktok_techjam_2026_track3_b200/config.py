@@ -1,4 +1,4 @@
-"""Shape records for the attention layer and the five BASELINE workloads.
+"""Shape records for the attention layer and the five benchmark workloads.
 
 ``LayerConfig`` mirrors the fields of the reference's ``TransformerConfig``
 (torch_transformer_benchmark.py:29-56) that the attention layer uses, plus the

@@ -124,7 +124,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // The k-th work item of this CTA: item indices are dealt out in rounds of
 // gridDim.x, alternating direction each round ("snake" order).  With items
 // sorted heaviest first this keeps the per-CTA totals within ~3% of the mean
-// for causal attention (plain striding: ~11% for BASELINE config 2).
+// for causal attention (plain striding: ~11% for benchmark configuration 2).
 __device__ __forceinline__ int item_of(int k) {
   return k * (int)gridDim.x + ((k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
 }

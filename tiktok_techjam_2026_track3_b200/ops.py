@@ -348,7 +348,7 @@ def int8_attn_layer(x: torch.Tensor, w_qkv8: torch.Tensor, s_qkv: torch.Tensor,
                     residual: Optional[torch.Tensor] = None, add_residual: bool = True,
                     out: Optional[torch.Tensor] = None,
                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """W8A8 attention layer (BASELINE config 3 recipe)."""
+    """W8A8 attention layer (benchmark configuration 3 recipe)."""
     lib = _lib.load()
     x = _cuda(x, "x")
     dt = _dtype_code(x)

@@ -1,7 +1,7 @@
 """Host-resident batches through a device module with the PCIe copies hidden.
 
 A serving loop whose activations live in host memory pays a host-to-device
-copy of every input and a device-to-host copy of every output; at BASELINE
+copy of every input and a device-to-host copy of every output; at benchmark
 config 2 (32 MiB each way per batch) those copies take longer than the three
 layer kernels.  ``HostPipeline`` overlaps them across batches: while batch i
 runs on the compute stream, batch i+1 is copied in on a second stream and
