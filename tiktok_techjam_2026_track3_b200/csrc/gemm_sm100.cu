@@ -234,7 +234,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       tmem_ld64(t_row + c * kEpiBoxCols, r);  // warp-collective
       if constexpr (kResidual) {
         const uint32_t ph = b ? es.phase1 : es.phase0;
-        if (!mbar_wait_warp(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
+        if (!mbar_wait_warp<true>(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
         if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
       }
 #pragma unroll
@@ -385,7 +385,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int m_blk = tile / p.num_n_blocks;
         const int n_blk = tile - m_blk * p.num_n_blocks;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) {
+          if (!mbar_wait<true>(&empty[stage], phase ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) {
             ok = false;
             break;
           }
@@ -413,14 +413,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutAccEmpty, abort_flag)) {
+        if (!mbar_wait<true>(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutAccEmpty, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.status, kDevTimeoutTmaFull, abort_flag)) {
+          if (!mbar_wait<true>(&full[stage], phase, p.status, kDevTimeoutTmaFull, abort_flag)) {
             ok = false;
             break;
           }
@@ -460,7 +460,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_warp(&acc_full[acc], acc_phase, p.status, kDevTimeoutAccFull, abort_flag)) break;
+      if (!mbar_wait_warp<true>(&acc_full[acc], acc_phase, p.status, kDevTimeoutAccFull, abort_flag)) break;
       tc_fence_after();
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;
@@ -568,7 +568,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const int m_blk = tile / p.num_n_blocks;
         const int n_blk = tile - m_blk * p.num_n_blocks;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) {
+          if (!mbar_wait<true>(&empty[stage], phase ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag)) {
             ok = false;
             break;
           }
@@ -599,14 +599,14 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       for (int tile = pair_id; ok && tile < num_tiles; tile += num_pairs, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutAccEmpty, abort_flag)) {
+        if (!mbar_wait<true>(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutAccEmpty, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.status, kDevTimeoutTmaFull, abort_flag)) {
+          if (!mbar_wait<true>(&full[stage], phase, p.status, kDevTimeoutTmaFull, abort_flag)) {
             ok = false;
             break;
           }
@@ -649,7 +649,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_warp(&acc_full[acc], acc_phase, p.status, kDevTimeoutAccFull, abort_flag)) break;
+      if (!mbar_wait_warp<true>(&acc_full[acc], acc_phase, p.status, kDevTimeoutAccFull, abort_flag)) break;
       tc_fence_after();
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;

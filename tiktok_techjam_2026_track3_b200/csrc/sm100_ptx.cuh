@@ -72,17 +72,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// As above, but the thread may be suspended up to `suspend_ns` waiting for the
+// phase (it resumes as soon as the phase completes): a waiter that is not on
+// the critical path stops competing for issue slots with the warps that are.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done) : "r"(bar), "r"(parity), "r"(suspend_ns) : "memory");
+  return done != 0;
+}
+constexpr uint32_t kSuspendNs = 1000000;  // per try; the loop's time limit still applies
+
 // Wait until the barrier phase with the given parity has completed.  Bounded:
 // returns false (and records `code`) after kWaitTimeoutNs, or at once when
 // another role has already flagged an abort in `*abort_flag`.
+// kSuspend: each try may suspend the thread (mbar_try_wait_suspend); with up
+// to kSuspendNs per try the time limit is checked at least every ~64 ms.
+template <bool kSuspend = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
                                           int code, volatile int* abort_flag,
                                           uint64_t limit_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
+  auto try_once = [&]() {
+    return kSuspend ? mbar_try_wait_suspend(a, parity, kSuspendNs) : mbar_try_wait(a, parity);
+  };
+  if (try_once()) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(a, parity)) return true;
+    if (try_once()) return true;
     if ((i & 63u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (global_timer_ns() - t0 > limit_ns) {
@@ -98,10 +118,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 // (.sync.aligned) tcgen05 instructions: every lane waits, then the lanes agree
 // (and reconverge) through __all_sync, so either the whole warp proceeds or
 // the whole warp gives up.
+template <bool kSuspend = false>
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status,
                                                int code, volatile int* abort_flag,
                                                uint64_t limit_ns = kWaitTimeoutNs) {
-  const bool ok = mbar_wait(bar, parity, status, code, abort_flag, limit_ns);
+  const bool ok = mbar_wait<kSuspend>(bar, parity, status, code, abort_flag, limit_ns);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
