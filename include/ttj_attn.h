@@ -264,6 +264,10 @@ int ttj_layernorm_fwd(const void* x, const void* gamma, const void* beta, const 
  * y[M,N] = gelu(x[M,K] . w[N,K]^T + bias[N]) with the exact (erf) GELU:
  * the block's F.gelu(self.ffn_in(...), approximate="none")
  * (torch_transformer_benchmark.py:141) as one GEMM with a fused epilogue.
+ * erf(z) is evaluated as 1 - erfc(z) with an erfc of fractional error below
+ * 1.2e-7 (Numerical Recipes' Chebyshev fit), so the 16-bit result is the
+ * correctly rounded exact GELU in almost every case and never more than one
+ * unit in the last place off.
  * Requires N % 32 == 0 and K % 8 == 0.
  */
 int ttj_linear_gelu_fwd(const void* x, const void* w, const void* bias, void* y, int64_t m,
