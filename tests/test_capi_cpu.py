@@ -122,3 +122,14 @@ def test_workspace_sizes():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(RuntimeError, match="not found"):
         _lib.load(tmp_path / "nope.so")
+
+
+def test_c_program_builds_against_the_abi(tmp_path):
+    """tests/c/layer_check.c, which drives the whole layer from C, compiles
+    with -Werror against include/ttj_attn.h and links against the library
+    (it runs in tests/test_gpu_capi_c.py)."""
+    from capi_c_build import build, toolchain_available
+    if not toolchain_available():
+        pytest.skip("gcc, the CUDA headers or the built library missing")
+    assert build(tmp_path).exists()
+
