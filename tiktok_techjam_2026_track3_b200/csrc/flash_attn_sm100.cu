@@ -222,6 +222,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dependency_wait();  // the previous kernel's writes (qkv) are visible from here
+  grid_launch_dependents();
 
   if (warp < 4) {
     setmaxnreg_dec<kRegsCtl>();
@@ -703,8 +705,7 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   }
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
   const int grid = p.num_items < sm_count() ? p.num_items : sm_count();
-  kern<<<grid, kThreads, L::kTotal, stream>>>(tm, tm_ctx, p);
-  TTJ_CUDA_TRY(cudaGetLastError());
+  TTJ_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), L::kTotal, stream, tm, tm_ctx, p));
   return TTJ_OK;
 }
 

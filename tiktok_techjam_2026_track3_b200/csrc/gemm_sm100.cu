@@ -369,6 +369,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dependency_wait();  // the previous kernel's writes are visible from here
+  grid_launch_dependents();
 
   const int num_tiles = p.num_m_blocks * p.num_n_blocks;
   const int num_kb = (p.K + kBK - 1) / kBK;
@@ -550,6 +552,8 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   cluster_sync();  // barriers of both CTAs initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dependency_wait();  // the previous kernel's writes are visible from here
+  grid_launch_dependents();
 
   const int num_tiles = p.num_m_blocks * p.num_n_blocks;   // m blocks of 256 rows
   const int num_kb = (p.K + kBK - 1) / kBK;
@@ -742,8 +746,7 @@ int launch_one(const GemmArgs& g, cudaStream_t stream) {
   const int grid = tiles < sm_count() ? tiles : sm_count();
   auto kern = gemm_tn_kernel<TIn, TOut, BN, STAGES, EPI>;
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
-  kern<<<grid, kGemmThreads, L::kTotal, stream>>>(ta, tb, tout, tres, p);
-  TTJ_CUDA_TRY(cudaGetLastError());
+  TTJ_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kGemmThreads), L::kTotal, stream, ta, tb, tout, tres, p));
   return TTJ_OK;
 }
 
@@ -758,8 +761,7 @@ int launch_pair(const GemmArgs& g, cudaStream_t stream) {
   const int grid = 2 * (tiles < max_pairs ? tiles : max_pairs);
   auto kern = gemm_tn_pair_kernel<TIn, TOut, BN, STAGES, EPI>;
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
-  kern<<<grid, kGemmThreads, L::kTotal, stream>>>(ta, tb, tout, tres, p);
-  TTJ_CUDA_TRY(cudaGetLastError());
+  TTJ_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kGemmThreads), L::kTotal, stream, ta, tb, tout, tres, p));
   return TTJ_OK;
 }
 

@@ -18,6 +18,8 @@ __global__ void __launch_bounds__(256)
 layernorm_kernel(const T* __restrict__ x, const T* __restrict__ gamma, const T* __restrict__ beta,
                  const uint8_t* __restrict__ row_mask, T* __restrict__ y, int64_t rows, int d,
                  float eps) {
+  grid_dependency_wait();  // x may be the previous kernel's output
+  grid_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int nvec = d / 8;
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x / 32);
@@ -85,11 +87,11 @@ layernorm_kernel(const T* __restrict__ x, const T* __restrict__ gamma, const T* 
 }
 
 template <typename T, int VPL>
-void launch_vpl(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask, void* y,
-                int64_t rows, int d, float eps, int grid, cudaStream_t stream) {
-  layernorm_kernel<T, VPL><<<grid, 256, 0, stream>>>(
-      static_cast<const T*>(x), static_cast<const T*>(gamma), static_cast<const T*>(beta), row_mask,
-      static_cast<T*>(y), rows, d, eps);
+cudaError_t launch_vpl(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask, void* y,
+                       int64_t rows, int d, float eps, int grid, cudaStream_t stream) {
+  return launch_pdl(layernorm_kernel<T, VPL>, dim3(grid), dim3(256), 0, stream, static_cast<const T*>(x),
+                    static_cast<const T*>(gamma), static_cast<const T*>(beta), row_mask, static_cast<T*>(y),
+                    rows, d, eps);
 }
 
 template <typename T>
@@ -98,11 +100,10 @@ int launch_t(const void* x, const void* gamma, const void* beta, const uint8_t* 
   const int64_t want = (rows + 7) / 8;
   const int64_t cap = (int64_t)sm_count() * 8;  // 8 CTAs of 8 warps per SM
   const int grid = (int)(want < cap ? want : cap);
-  if (d <= 1024) launch_vpl<T, 4>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream);
-  else if (d <= 2048) launch_vpl<T, 8>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream);
-  else if (d <= 4096) launch_vpl<T, 16>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream);
-  else launch_vpl<T, 32>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream);
-  TTJ_CUDA_TRY(cudaGetLastError());
+  if (d <= 1024) TTJ_CUDA_TRY((launch_vpl<T, 4>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream)));
+  else if (d <= 2048) TTJ_CUDA_TRY((launch_vpl<T, 8>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream)));
+  else if (d <= 4096) TTJ_CUDA_TRY((launch_vpl<T, 16>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream)));
+  else TTJ_CUDA_TRY((launch_vpl<T, 32>(x, gamma, beta, row_mask, y, rows, d, eps, grid, stream)));
   return TTJ_OK;
 }
 

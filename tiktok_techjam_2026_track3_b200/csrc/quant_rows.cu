@@ -15,6 +15,8 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 quant_rows_kernel(const T* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scale,
                   int64_t rows, int64_t cols) {
+  grid_dependency_wait();  // x may be the previous kernel's output
+  grid_launch_dependents();
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x / 32);
   const int lane = threadIdx.x & 31;
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); row < rows;
@@ -63,11 +65,11 @@ int launch_quant_rows(const void* x, int8_t* q, float* scale, int64_t rows, int6
   const int64_t cap = (int64_t)sm_count() * 8;  // 8 CTAs of 8 warps per SM
   const int grid = (int)(want < cap ? want : cap);
   if (dtype == TTJ_F16)
-    quant_rows_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<const __half*>(x), q, scale, rows, cols);
+    TTJ_CUDA_TRY(launch_pdl(quant_rows_kernel<__half>, dim3(grid), dim3(threads), 0, stream,
+                            static_cast<const __half*>(x), q, scale, rows, cols));
   else
-    quant_rows_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), q, scale, rows, cols);
-  TTJ_CUDA_TRY(cudaGetLastError());
+    TTJ_CUDA_TRY(launch_pdl(quant_rows_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, stream,
+                            static_cast<const __nv_bfloat16*>(x), q, scale, rows, cols));
   return TTJ_OK;
 }
 

@@ -57,6 +57,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// Programmatic dependent launch.  Kernels of this library are launched so that
+// they may start while the previous kernel on the stream is still finishing
+// (launch_pdl on the host).  Each calls grid_dependency_wait() before its
+// first global-memory access of any kind -- it returns once the previous grid
+// has completed and its writes are visible, so reads see its results and
+// writes cannot overtake its reads -- and grid_launch_dependents() once every
+// CTA of its own grid is resident, so that the next kernel's CTAs can set up
+// (barriers, tensor memory) on SMs this grid leaves idle.  Both are no-ops for
+// a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];"
                ::"r"(smem_u32(bar)) : "memory");

@@ -33,6 +33,26 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Launch a kernel of this library with programmatic stream serialisation: it
+// may begin while the previous kernel on `stream` finishes, and waits for it
+// on the device (grid_dependency_wait() in sm100_ptx.cuh) before touching
+// global memory.  Works under CUDA-graph capture.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Encode a tiled TMA descriptor with 128-byte swizzle, zero out-of-bounds fill.
 // dims/strides are innermost-first; strides in bytes for dims 1..rank-1.
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
