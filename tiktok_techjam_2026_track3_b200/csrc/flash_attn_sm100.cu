@@ -502,7 +502,15 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         }
         const int k0 = j * kBN;
         const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && k0 + kBN - 1 > q0) || kmask != nullptr;
-        if (need_mask) {
+        if (CAUSAL && need_mask && kmask == nullptr && k0 + kBN <= p.S) {
+          // Causal limit only (the diagonal key tile): key k0 + i is visible
+          // to this row iff i <= q_row - k0.  One compare and one select per
+          // score; the general path below measured ~2.5K cycles per diagonal
+          // step, about 7% of the causal kernel for benchmark configuration 2.
+          const int lim = q_row - k0;
+#pragma unroll
+          for (int i = 0; i < kBN; ++i) s[i] = i <= lim ? s[i] : -INFINITY;
+        } else if (need_mask) {
           // Validity bits for the tile's keys, built cooperatively: lane l reads
           // keys l, l+32, l+64, l+96, one ballot per group of 32.
           uint32_t vbits[4];
