@@ -55,6 +55,7 @@ constexpr uint32_t kRegsCtl = 88;
 constexpr uint32_t kRegsSoftmax = 208;
 static_assert(kRegsCtl + 2 * kRegsSoftmax == 3 * kLaunchRegs, "register split must use the launch budget");
 constexpr uint32_t kTmemCols = 512;
+constexpr int64_t kHeadMajorKvBytes = int64_t(96) << 20;
 
 struct AttnParams {
   void* ctx;
@@ -62,6 +63,7 @@ struct AttnParams {
   int B, S, H, D;
   int num_pairs;     // ceil(S / 256)
   int num_items;     // B * H * num_pairs
+  int head_major;    // item order: 1 = a head's pairs consecutive, 0 = pair index outermost
   float scale_log2;  // head_dim^-0.5 * log2(e)
   int* status;
 };
@@ -129,18 +131,29 @@ __device__ __forceinline__ int item_of(int k) {
   return k * (int)gridDim.x + ((k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
 }
 
-// Decode work item -> (b, h, pair).  Causal items are ordered by decreasing
-// pair index (longest key range first).
+// Decode work item -> (b, h, pair).  Causal pairs come in decreasing pair
+// index (longest key range first).  Pair-major order (the pair index
+// outermost) keeps the whole grid on items of equal length, which balances
+// short sequences best.  Head-major order (a head's pairs consecutive) is used
+// when every head's K and V together exceed what L2 can hold: the CTAs then
+// running work on a few heads and read their K/V tiles from L2 instead of
+// each streaming its own head's from DRAM.
 struct Item {
   int b, h, pair;
 };
 template <bool CAUSAL>
 __device__ __forceinline__ Item decode_item(int item, const AttnParams& p) {
-  const int bh_count = p.B * p.H;
-  const int round = item / bh_count;
-  const int bh = item - round * bh_count;
+  int bh, r;
+  if (p.head_major) {
+    bh = item / p.num_pairs;
+    r = item - bh * p.num_pairs;
+  } else {
+    const int bh_count = p.B * p.H;
+    r = item / bh_count;
+    bh = item - r * bh_count;
+  }
   Item it;
-  it.pair = CAUSAL ? p.num_pairs - 1 - round : round;
+  it.pair = CAUSAL ? p.num_pairs - 1 - r : r;
   it.b = bh / p.H;
   it.h = bh - it.b * p.H;
   return it;
@@ -698,6 +711,8 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   p.D = (int)D;
   p.num_pairs = (int)((a.seq_len + 2 * kBM - 1) / (2 * kBM));
   const int64_t items = a.batch * a.num_heads * (int64_t)p.num_pairs;
+  // K and V of every head (2 x S x head_dim x 2 bytes each) against ~3/4 of the 126 MB L2.
+  p.head_major = a.batch * a.num_heads * a.seq_len * HD * 4 > kHeadMajorKvBytes ? 1 : 0;
   if (items >= (int64_t)1 << 31) return fail(TTJ_ERR_UNSUPPORTED, "too many attention work items");
   p.num_items = (int)items;
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
