@@ -14,7 +14,7 @@ d=1024, Project/research/quantization-tolerance.md:8-10)."""
 import pytest
 import torch
 
-from oracle import (LayerWeights, attention_layer_ref, compare_outputs, generate_case,
+from oracle import (LayerWeights, attention_layer_ref, compare_outputs, generate_case, quant_rows_ref,
                     int8_attention_layer_ref, int8_linear_ref, make_weights)
 from tiktok_techjam_2026_track3_b200 import B200AttentionLayer, ops
 
@@ -77,3 +77,29 @@ def test_int8_layer_stagewise(B, S, D, H, causal):
     e2e_fp32 = compare_outputs(attention_layer_ref(x, wb, H, None, causal, batch_chunk=1), out.float())
     print(f"\nint8 B{B} S{S} D{D}: vs recipe(fp32 attn) {e2e_recipe}; vs fp32 layer {e2e_fp32}")
     assert e2e_recipe.max_abs_error < 0.1 and e2e_recipe.mean_abs_error < 5e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("cols", [8, 1000, 1024, 2048, 4096, 4104])
+def test_quant_rows_bit_exact_on_adversarial_rows(dtype, cols):
+    """The per-token quantiser against the recipe's IEEE division and round-half-even
+    (oracle quant_rows_ref, evaluated on the CPU), bit for bit, on rows built to reach
+    its edge cases: every 16-bit bit pattern (finite), fp32-subnormal values (bf16),
+    all-zero rows (the 1e-6 clamp), constant rows, values on half-integer quotients,
+    and lengths that use each of the kernel's register paths and the two-pass path."""
+    g = torch.Generator().manual_seed(cols)
+    rows = 257
+    bits = torch.randint(-32768, 32768, (rows, cols), generator=g, dtype=torch.int16)
+    x = bits.view(dtype)
+    x = torch.where(torch.isfinite(x), x, torch.zeros_like(x))
+    x[1] = 0
+    x[2] = 3.0
+    if dtype == torch.bfloat16:
+        x[3] = (torch.randn(cols, generator=g) * 1e-39).to(dtype)  # fp32-subnormal values
+    x[4] = (torch.arange(cols) % 254 - 126.5).to(dtype)        # row max 127 -> scale 1:
+    x[4, 0] = 127.0                                             # every quotient a tie k + 1/2
+    x[5] = torch.randn(cols, generator=g).to(dtype) * 1e4
+    q, s = ops.int8_quant_rows(x.cuda())
+    q_ref, s_ref = quant_rows_ref(x.float())
+    assert torch.equal(s.cpu(), s_ref)
+    assert torch.equal(q.cpu(), q_ref)
