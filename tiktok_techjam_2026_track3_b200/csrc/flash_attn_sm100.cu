@@ -79,12 +79,12 @@ struct AttnSmem {
   static constexpr int kQOff = 0;                   // [kQBufs][Q_A, Q_B]
   static constexpr int kKOff = 2 * kQBufs * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  // head_dim 64: the context rows leave through a TMA store from a 4 KB
-  // staging box per softmax warp (32 rows x 128 bytes, 128-byte swizzle);
-  // measured: per-thread 16-byte row stores took 1-2.5K cycles per item end.
-  static constexpr bool kTmaEpi = HD == 64;
+  // The context rows leave through TMA stores from a 4 KB staging box per
+  // softmax warp (32 rows x 64 columns, 128-byte swizzle; head_dim 128 reuses
+  // it for its second 64 columns); measured: per-thread 16-byte row stores took
+  // 1-2.5K cycles per item end at head_dim 64, ~3.5K at head_dim 128.
   static constexpr int kEpiOff = kVOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kEpiOff + (kTmaEpi ? 8 * 32 * 128 : 0);
+  static constexpr int kBarOff = kEpiOff + 8 * 32 * 128;
   static constexpr int kTotal = 1024 + kBarOff + 512;
   static_assert(kTotal <= 232448, "shared memory budget");
   // TMEM columns
@@ -623,15 +623,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       od_phase ^= 1u;
       tc_fence_after();
       const float inv_l = 1.f / l_run;
-      if constexpr (L::kTmaEpi) {
-        // this warp's 32 rows x 64 columns: swizzled staging box, one TMA store
-        uint8_t* box = smem + L::kEpiOff + (warp - 4) * (32 * 128);
-        if (lane == 0) bulk_wait_group_read<0>();  // the previous item's store has read the box
+      // this warp's 32 rows, 64 columns at a time: swizzled staging box, one
+      // TMA store each (the box is reused once the previous store has read it)
+      uint8_t* box = smem + L::kEpiOff + (warp - 4) * (32 * 128);
+#pragma unroll
+      for (int hh = 0; hh < HD / 64; ++hh) {
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
-          tmem_ld32(t_o + c * 32, o);
+          tmem_ld32(t_o + hh * 64 + c * 32, o);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 w;
@@ -646,33 +648,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&tm_ctx, box, it.h * HD, q0 + lg * 32, it.b);  // rows >= S are clipped
+          tma_store_3d(&tm_ctx, box, it.h * HD + 64 * hh, q0 + lg * 32, it.b);  // rows >= S are clipped
           bulk_commit_group();
-        }
-        continue;
-      }
-      T* dst = static_cast<T*>(p.ctx) + ((int64_t)it.b * p.S + q_row) * p.D + it.h * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(t_o + c * 32, o);
-        if (q_row < p.S) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = Pack<T>::two(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
-            w.y = Pack<T>::two(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
-            w.z = Pack<T>::two(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
-            w.w = Pack<T>::two(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
-            d4[q] = w;
-          }
         }
       }
       // The next item's first P.V overwrites O_t only after this thread's next
-      // p_full arrival, which follows these loads.
+      // p_full arrival, which follows these TMEM loads.
     }
-    if (L::kTmaEpi && lane == 0) bulk_wait_group_all();  // context stores complete before exit
+    if (lane == 0) bulk_wait_group_all();  // context stores complete before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -692,16 +675,15 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                        3, a.qkv, dims, strides, box);
   if (rc) return rc;
-  CUtensorMap tm_ctx = tm;  // unused unless L::kTmaEpi
-  if (L::kTmaEpi) {
-    const uint64_t cdims[3] = {(uint64_t)D, (uint64_t)a.seq_len, (uint64_t)a.batch};
-    const uint64_t cstrides[2] = {(uint64_t)(D * 2), (uint64_t)(a.seq_len * D * 2)};
-    const uint32_t cbox[3] = {64, 32, 1};
-    rc = encode_tmap(&tm_ctx, std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                     3, a.ctx, cdims, cstrides, cbox);
-    if (rc) return rc;
-  }
+  // ctx [B, S, D]: the epilogue's 32-row x 64-column boxes
+  CUtensorMap tm_ctx;
+  const uint64_t cdims[3] = {(uint64_t)D, (uint64_t)a.seq_len, (uint64_t)a.batch};
+  const uint64_t cstrides[2] = {(uint64_t)(D * 2), (uint64_t)(a.seq_len * D * 2)};
+  const uint32_t cbox[3] = {64, 32, 1};
+  rc = encode_tmap(&tm_ctx, std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   3, a.ctx, cdims, cstrides, cbox);
+  if (rc) return rc;
   AttnParams p;
   p.ctx = a.ctx;
   p.key_mask = a.key_mask;
