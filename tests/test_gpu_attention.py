@@ -93,6 +93,24 @@ def test_flash_key_mask(dt, kind, B, S, H, hd, causal):
     check_ctx(qkv, H, causal, ctx, mask)
 
 
+@pytest.mark.parametrize("B,S,H,hd,causal", [(2, 2048, 4, 64, True), (2, 1000, 2, 128, False),
+                                             (1, 512, 2, 128, True)])
+def test_flash_all_true_mask_equals_no_mask(B, S, H, hd, causal):
+    """The reference's benchmark passes an all-true valid_token_mask for unpadded
+    inputs (torch_transformer_benchmark.py:255-259); the kernel must give exactly
+    the maskless result (it skips the per-score masking when every key of a tile
+    is valid), and a mask that drops keys must still change the result."""
+    qkv = make_qkv(B, S, H, hd, "bf16", 5 + S)
+    ones = torch.ones(B, S, dtype=torch.bool, device="cuda")
+    ref = ops.flash_attn(qkv, H, causal)
+    assert torch.equal(ops.flash_attn(qkv, H, causal, key_mask=ones), ref)
+    part = ones.clone()
+    part[:, S // 2 + 1:] = False
+    out = ops.flash_attn(qkv, H, causal, key_mask=part)
+    check_ctx(qkv, H, causal, out, part)
+    assert not torch.equal(out, ref)
+
+
 @pytest.mark.parametrize("S,H,hd", [(100000, 2, 64), (262144, 1, 128)])
 def test_flash_long_sequence_stripes(S, H, hd):
     """Long-context shapes (configs 4 and 5 per head): sampled query stripes

@@ -514,19 +514,15 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           mbar_arrive(&s_free[t]);  // the tensor core may overwrite S_t now
         }
         const int k0 = j * kBN;
-        const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && k0 + kBN - 1 > q0) || kmask != nullptr;
-        if (CAUSAL && need_mask && kmask == nullptr && k0 + kBN <= p.S) {
-          // Causal limit only (the diagonal key tile): key k0 + i is visible
-          // to this row iff i <= q_row - k0.  One compare and one select per
-          // score; the general path below measured ~2.5K cycles per diagonal
-          // step, about 7% of the causal kernel for benchmark configuration 2.
-          const int lim = q_row - k0;
-#pragma unroll
-          for (int i = 0; i < kBN; ++i) s[i] = i <= lim ? s[i] : -INFINITY;
-        } else if (need_mask) {
-          // Validity bits for the tile's keys, built cooperatively: lane l reads
-          // keys l, l+32, l+64, l+96, one ballot per group of 32.
-          uint32_t vbits[4];
+        // Which of the tile's 128 keys this row may see: keys past S, keys the
+        // key mask drops, and (causal) keys after the query are masked to -inf.
+        const bool tail = k0 + kBN > p.S;
+        const bool diag = CAUSAL && k0 + kBN - 1 > q0;  // the tile straddles the diagonal
+        // Validity bits of the tile's keys (key < S and, with a key mask, its
+        // byte set), built cooperatively: lane l reads keys l, l+32, l+64,
+        // l+96, one ballot per group of 32.  Warp-uniform.
+        uint32_t vbits[4] = {~0u, ~0u, ~0u, ~0u};
+        if (tail || kmask != nullptr) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const int key = k0 + g * 32 + lane;
@@ -534,6 +530,19 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
             if (v && kmask != nullptr) v = kmask[key] != 0;
             vbits[g] = __ballot_sync(0xffffffffu, v);
           }
+        }
+        if ((vbits[0] & vbits[1] & vbits[2] & vbits[3]) == ~0u) {
+          // Every key valid (no mask, or an all-true mask such as the
+          // benchmark's unpadded inputs): only the causal limit can apply.
+          // Key k0 + i is visible to this row iff i <= q_row - k0: one compare
+          // and one select per score.  (The general path below measured
+          // ~2.5K cycles per step.)
+          if (diag) {
+            const int lim = q_row - k0;
+#pragma unroll
+            for (int i = 0; i < kBN; ++i) s[i] = i <= lim ? s[i] : -INFINITY;
+          }
+        } else {
 #pragma unroll
           for (int i = 0; i < kBN; ++i) {
             bool v = (vbits[i >> 5] >> (i & 31)) & 1u;
