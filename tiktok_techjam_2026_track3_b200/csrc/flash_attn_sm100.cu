@@ -496,6 +496,16 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       const int q0 = it.pair * 2 * kBM + t * kBM;
       const int q_row = q0 + r;
       const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
+      // Key-mask bytes of the current key tile (lane l: keys l, l+32, l+64,
+      // l+96), loaded one step ahead so the load overlaps the previous step.
+      uint32_t mbyte[4] = {0u, 0u, 0u, 0u};
+      if (kmask != nullptr) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int key = g * 32 + lane;
+          mbyte[g] = key < p.S ? __ldg(kmask + key) : 0u;
+        }
+      }
       float m_run = -INFINITY;  // exponent reference (log2 units), moved lazily
       float l_run = 0.f;        // running sum of P in fp32
       for (int j = 0; j < n_kv; ++j) {
@@ -519,7 +529,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         const bool tail = k0 + kBN > p.S;
         const bool diag = CAUSAL && k0 + kBN - 1 > q0;  // the tile straddles the diagonal
         // Validity bits of the tile's keys (key < S and, with a key mask, its
-        // byte set), built cooperatively: lane l reads keys l, l+32, l+64,
+        // byte set), built cooperatively: lane l holds keys l, l+32, l+64,
         // l+96, one ballot per group of 32.  Warp-uniform.
         uint32_t vbits[4] = {~0u, ~0u, ~0u, ~0u};
         if (tail || kmask != nullptr) {
@@ -527,8 +537,15 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           for (int g = 0; g < 4; ++g) {
             const int key = k0 + g * 32 + lane;
             bool v = key < p.S;
-            if (v && kmask != nullptr) v = kmask[key] != 0;
+            if (kmask != nullptr) v = v && mbyte[g] != 0u;
             vbits[g] = __ballot_sync(0xffffffffu, v);
+          }
+          if (kmask != nullptr && j + 1 < n_kv) {  // the next tile's bytes
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int key = k0 + kBN + g * 32 + lane;
+              mbyte[g] = key < p.S ? __ldg(kmask + key) : 0u;
+            }
           }
         }
         if ((vbits[0] & vbits[1] & vbits[2] & vbits[3]) == ~0u) {
