@@ -26,8 +26,9 @@
  *   ctx         [B, S, D]     attention context with heads already merged
  *   valid_token_mask [B, S]   uint8 (torch.bool), 1 = valid; may be NULL (all valid)
  *
- * Supported: dtype fp16 or bf16; head_dim 64 or 128; D a multiple of 64;
- * any B >= 1, S >= 1.  Anything else returns TTJ_ERR_UNSUPPORTED.
+ * Supported: dtype fp16 or bf16; head_dim a multiple of 8 up to 256; D a
+ * multiple of 32; any B >= 1, 1 <= S <= 8388480.  Anything else returns
+ * TTJ_ERR_UNSUPPORTED.
  */
 #ifndef TTJ_ATTN_H_
 #define TTJ_ATTN_H_
@@ -184,7 +185,12 @@ int ttj_attn_layer_fwd(const ttj_attn_layer_args* args, ttj_stream_t stream);
  * One array per GPU, shared by every call: calls that overlap on the same GPU
  * race; calls ordered on one stream are safe.  The first call on a device
  * looks up the array's address with that device current; make it before any
- * stream capture.  Every GPU that loads the library holds the array until exit.
+ * stream capture.  Because the CUDA runtime loads device code lazily, that
+ * first call is also when the array is mapped: it grows device memory by
+ * 32 MiB once (TTJ_ERR_CUDA if the device has no 32 MiB free), so a caller
+ * that reserves the rest of device memory up front makes it during start-up,
+ * before the reservation.  From then on the device holds the array until the
+ * process exits and calls map nothing more.
  */
 int ttj_attn_layer_fwd_noalloc(const ttj_attn_layer_args* args, ttj_stream_t stream);
 

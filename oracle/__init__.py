@@ -20,6 +20,7 @@ from .attention_ref import (  # noqa: F401
     AccuracyReport,
     LayerWeights,
     attention_layer_ref,
+    attention_layer_rows_ref,
     attention_layer_streamed_ref,
     compare_outputs,
     generate_case,

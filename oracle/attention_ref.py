@@ -23,6 +23,7 @@ __all__ = [
     "AccuracyReport",
     "LayerWeights",
     "attention_layer_ref",
+    "attention_layer_rows_ref",
     "attention_layer_streamed_ref",
     "compare_outputs",
     "generate_case",
@@ -164,7 +165,8 @@ def streamed_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            scale: float, causal: bool,
                            key_mask: Optional[torch.Tensor] = None,
                            q_rows: Optional[torch.Tensor] = None,
-                           k_chunk: int = 8192) -> torch.Tensor:
+                           k_chunk: int = 8192,
+                           probs_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
     """Online-softmax fp32 attention for one (batch, head) slice, no S×S table.
 
     q: [Sq,hd] (the query rows to evaluate), k/v: [S,hd]; ``q_rows`` gives the
@@ -172,7 +174,14 @@ def streamed_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     a sampled stripe of a long sequence can be evaluated on its own.  The
     behaviour follows the reference's long-context checker
     ``Project/tools/shape14_eval.py:201-236``: running max / running sum over
-    key chunks, rescaled accumulator, one division at the end."""
+    key chunks, rescaled accumulator, one division at the end.
+
+    ``probs_dtype`` rounds the normalised probabilities to that dtype before
+    they multiply v, as the reference's 16-bit run does with
+    ``softmax(scores.float()).to(x.dtype)`` (torch_transformer_benchmark.py:111).
+    Rounding needs each row's final max and sum first, so that variant makes
+    two passes over the keys: the online pass above for max and sum, then
+    p = round(exp(s - max) / sum) and the product with v."""
     qf, kf, vf = q.float(), k.float(), v.float()
     Sq = qf.shape[0]
     S = kf.shape[0]
@@ -183,22 +192,86 @@ def streamed_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     run_sum = torch.zeros(Sq, device=q.device)
     acc = torch.zeros(Sq, vf.shape[1], device=q.device)
     k_end = int(q_rows.max().item()) + 1 if causal else S
-    for k0 in range(0, k_end, k_chunk):
-        k1 = min(k0 + k_chunk, k_end)
+
+    def scores(k0, k1):
         s = (qf @ kf[k0:k1].T) * scale
         kidx = torch.arange(k0, k1, device=q.device)
         if causal:
             s = s.masked_fill(kidx[None, :] > q_rows[:, None], float("-inf"))
         if key_mask is not None:
             s = s.masked_fill(~key_mask[k0:k1][None, :], float("-inf"))
+        return s
+
+    for k0 in range(0, k_end, k_chunk):
+        k1 = min(k0 + k_chunk, k_end)
+        s = scores(k0, k1)
         new_max = torch.maximum(run_max, s.amax(dim=1))
         safe = torch.where(torch.isinf(new_max), torch.zeros_like(new_max), new_max)
         alpha = torch.exp(run_max - safe)
         p = torch.exp(s - safe[:, None])
         run_sum = run_sum * alpha + p.sum(dim=1)
-        acc = acc * alpha[:, None] + p @ vf[k0:k1]
+        if probs_dtype is None:
+            acc = acc * alpha[:, None] + p @ vf[k0:k1]
         run_max = new_max
-    return acc / run_sum[:, None]
+    if probs_dtype is None:
+        return acc / run_sum[:, None]
+    safe = torch.where(torch.isinf(run_max), torch.zeros_like(run_max), run_max)
+    for k0 in range(0, k_end, k_chunk):
+        k1 = min(k0 + k_chunk, k_end)
+        p = torch.exp(scores(k0, k1) - safe[:, None]) / run_sum[:, None]
+        acc = acc + p.to(probs_dtype).float() @ vf[k0:k1]
+    return acc
+
+
+def attention_layer_rows_ref(x: torch.Tensor, w: LayerWeights, num_heads: int, causal: bool,
+                             batches: Sequence[int], q_rows: torch.Tensor,
+                             store_dtypes: Sequence[Optional[torch.dtype]] = (None,),
+                             valid_token_mask: Optional[torch.Tensor] = None,
+                             k_chunk: int = 16384) -> List[torch.Tensor]:
+    """Layer OUTPUT rows ``x + BaselineSelfAttention(x)`` for sampled batch rows
+    and query rows, on x's device, one result [len(batches), len(q_rows), D]
+    (fp32) per entry of ``store_dtypes``.
+
+    ``None`` evaluates Ref:85-122 + :140 in fp32 throughout: the exact layer for
+    the given (already rounded) inputs and weights.  A 16-bit dtype rounds to it
+    where the reference's own 16-bit run stores a tensor -- q, k and v after the
+    projections (Ref:93-95), the probabilities (Ref:111), the context after the
+    head merge (Ref:112-117), the out-proj output (Ref:118) and the residual sum
+    (Ref:140) -- except the score matrix, which the reference's 16-bit run also
+    rounds but which this checker (like the kernel) keeps in fp32.  Every
+    variant shares the fp32 projections, so their differences are exactly the
+    roundings.  Only the sampled query rows and the keys they can see are
+    computed, which lets sequences of 10^5 - 2.6*10^5 tokens be checked stripe by
+    stripe."""
+    B, S, D = x.shape
+    hd = D // num_heads
+    wf = w.to(dtype=torch.float32, device=x.device)
+    q_rows = q_rows.to(x.device)
+    k_end = int(q_rows.max().item()) + 1 if causal else S
+    outs = [torch.empty(len(batches), len(q_rows), D, device=x.device) for _ in store_dtypes]
+
+    def rnd(t, dt):
+        return t if dt is None else t.to(dt).float()
+
+    for bi, b in enumerate(batches):
+        xb = x[b, :k_end].float()
+        km = None if valid_token_mask is None else valid_token_mask[b].to(x.device)
+        ctx = [torch.empty(len(q_rows), D, device=x.device) for _ in store_dtypes]
+        for h in range(num_heads):
+            sl = slice(h * hd, (h + 1) * hd)
+            q = _linear(xb[q_rows], wf.wq[sl], wf.bq[sl])
+            k = _linear(xb, wf.wk[sl], wf.bk[sl])
+            v = _linear(xb, wf.wv[sl], wf.bv[sl])
+            for i, dt in enumerate(store_dtypes):
+                ctx[i][:, sl] = streamed_attention_ref(rnd(q, dt), rnd(k, dt), rnd(v, dt), hd ** -0.5, causal,
+                                                       key_mask=km, q_rows=q_rows, k_chunk=k_chunk,
+                                                       probs_dtype=dt)
+        for i, dt in enumerate(store_dtypes):
+            o = rnd(_linear(rnd(ctx[i], dt), wf.wo, wf.bo), dt)
+            if km is not None:
+                o = o.masked_fill(~km[q_rows][:, None], 0)
+            outs[i][bi] = rnd(xb[q_rows] + o, dt)
+    return outs
 
 
 def attention_layer_streamed_ref(x: torch.Tensor, w: LayerWeights, num_heads: int,

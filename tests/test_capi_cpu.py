@@ -71,9 +71,19 @@ def test_argument_validation_without_device():
     assert b"multiple of 32" in lib.ttj_last_error()
     # misaligned pointer
     assert lib.ttj_linear_fwd(fake + 2, fake, fake, None, None, fake, 4, 32, 8, 0, None, None) == -3
-    # head_dim 96 unsupported
-    assert lib.ttj_flash_attn_fwd(fake, None, fake, 1, 16, 2, 96, 1, 0, None, None) == -2
+    # head_dim must be a multiple of 8 and at most 256 (12 and 264 are not)
+    assert lib.ttj_flash_attn_fwd(fake, None, fake, 1, 16, 8, 12, 1, 0, None, None) == -2
     assert b"head_dim" in lib.ttj_last_error()
+    assert lib.ttj_flash_attn_fwd(fake, None, fake, 1, 16, 2, 264, 1, 0, None, None) == -2
+    assert b"head_dim" in lib.ttj_last_error()
+    # d_model must be a multiple of 32 (head_dim 8 over 3 heads: d_model 24)
+    assert lib.ttj_flash_attn_fwd(fake, None, fake, 1, 16, 3, 8, 1, 0, None, None) == -2
+    assert b"multiple of 32" in lib.ttj_last_error()
+    # factors beyond the limits are rejected before any product is formed (no wrap-around)
+    assert lib.ttj_flash_attn_fwd(fake, None, fake, (1 << 57) + 1, 128, 4, 32, 1, 0, None, None) == -2
+    assert lib.ttj_flash_attn_fwd(fake, None, fake, 1 << 30, 1 << 22, 32, 128, 1, 0, None, None) == -2
+    assert b"too large" in lib.ttj_last_error()
+    assert lib.ttj_attn_layer_workspace_size((1 << 57) + 1, 128, 128, 0) == 0
     # d_model not divisible by heads via the layer entry point
     a = _lib.AttnLayerArgs(x=fake, w_qkv=fake, b_qkv=fake, w_o=fake, b_o=fake, out=fake * 2,
                            workspace=fake, workspace_bytes=1 << 40, batch=1, seq_len=8,

@@ -8,6 +8,7 @@ import pytest
 import torch
 
 from oracle import compare_outputs, streamed_attention_ref
+from parity_util import no_worse_than_reference_rounding
 from tiktok_techjam_2026_track3_b200 import ops
 
 pytestmark = pytest.mark.gpu
@@ -37,21 +38,19 @@ def dense_ref(qkv, H, causal, key_mask=None, probs_dtype=None):
 def check_ctx(qkv, H, causal, ctx, key_mask=None):
     """fp16: the reference predicate (abs 2e-3 OR rel 2e-2) against fp32.
     bf16: bf16 keeps 8 significant bits, so rounding each probability costs up
-    to 2^-9 of it and a context entry can move by ~2^-9 * max|v| (~1e-2 for
-    the N(0,1) values used here) -- the reference's own bf16 run has the same
-    error.  The gate is therefore: within abs 1e-2 OR rel 2e-2 of fp32, and no
-    worse than twice the reference-style rounding error (+1e-3)."""
+    to 2^-9 of it and a context entry can move by ~2^-9 * max|v| (~1e-2 for the
+    N(0,1) values used here), which the reference's own bf16 run does too
+    (probabilities rounded to bf16, torch_transformer_benchmark.py:111).  The
+    gate is the predicate against fp32 wherever that reference-style result
+    meets it, and otherwise no more failures and no larger errors than it has
+    (parity_util.no_worse_than_reference_rounding)."""
     ref = dense_ref(qkv, H, causal, key_mask)
     if qkv.dtype == torch.float16:
         rep = compare_outputs(ref, ctx.float())
         assert rep.passed, str(rep)
         return
-    rep = compare_outputs(ref, ctx.float(), atol=1e-2)
-    assert rep.passed, str(rep)
-    ref_style = dense_ref(qkv, H, causal, key_mask, probs_dtype=torch.bfloat16).to(torch.bfloat16)
-    err_ours = float((ctx.float() - ref).abs().max())
-    err_refstyle = float((ref_style.float() - ref).abs().max())
-    assert err_ours <= 2 * err_refstyle + 1e-3, (err_ours, err_refstyle)
+    ref_style = dense_ref(qkv, H, causal, key_mask, probs_dtype=torch.bfloat16).to(torch.bfloat16).float()
+    no_worse_than_reference_rounding(ref, ctx.float(), ref_style, f"bf16 attention {tuple(qkv.shape)} H{H}")
 
 
 def make_qkv(B, S, H, hd, dt, seed):
@@ -63,6 +62,11 @@ CASES = [  # (B, S, H, hd, causal)
     (1, 1, 1, 64, True), (2, 77, 2, 64, False), (1, 128, 1, 64, True), (2, 200, 4, 64, True),
     (1, 129, 1, 128, False), (3, 333, 2, 128, True), (1, 1000, 2, 128, False),
     (2, 2048, 16, 64, True), (1, 4096, 2, 128, True), (2, 1024, 4, 64, False),
+    # head_dim below / between / above the padded kernel sizes (zero-padded columns):
+    # 8 and 32 (the reference's shapes.json with d_model 32 / 128), 256 (d_model 1024 over 4 heads)
+    (3, 128, 4, 8, True), (2, 300, 16, 8, False), (4, 128, 4, 32, True), (2, 1000, 3, 32, False),
+    (2, 33, 2, 16, True), (2, 500, 2, 96, True), (4, 128, 4, 256, True), (1, 700, 2, 256, False),
+    (2, 1100, 2, 256, True), (1, 300, 2, 200, True), (1, 32, 4, 32, True),
 ]
 
 
@@ -78,7 +82,8 @@ def test_flash_matches_dense(dt, B, S, H, hd, causal):
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
 @pytest.mark.parametrize("kind", ["prefix", "random"])
 @pytest.mark.parametrize("B,S,H,hd,causal", [(3, 200, 2, 64, True), (2, 300, 2, 128, False),
-                                             (2, 1024, 4, 64, True)])
+                                             (2, 1024, 4, 64, True), (3, 128, 4, 32, True),
+                                             (2, 400, 2, 256, True)])
 def test_flash_key_mask(dt, kind, B, S, H, hd, causal):
     qkv = make_qkv(B, S, H, hd, dt, 77 + S)
     g = torch.Generator().manual_seed(S)
@@ -125,9 +130,10 @@ def test_flash_long_sequence_stripes(S, H, hd):
         v = qkv[0, :, 2 * D + h * hd:2 * D + (h + 1) * hd]
         ref = streamed_attention_ref(q[rows.cuda()], k, v, hd ** -0.5, True, q_rows=rows.cuda(),
                                      k_chunk=16384)
+        ref_style = streamed_attention_ref(q[rows.cuda()], k, v, hd ** -0.5, True, q_rows=rows.cuda(),
+                                           k_chunk=16384, probs_dtype=torch.bfloat16).to(torch.bfloat16)
         got = ctx[0, rows.cuda(), h * hd:(h + 1) * hd].float()
-        rep = compare_outputs(ref, got, atol=1e-2)  # bf16 probabilities, see check_ctx
-        assert rep.passed, f"head {h}: {rep}"
+        no_worse_than_reference_rounding(ref, got, ref_style.float(), f"S{S} head {h}")  # see check_ctx
     ops.check_device_status(qkv.device)
 
 

@@ -16,14 +16,16 @@ import torch
 
 from oracle import (LayerWeights, attention_layer_ref, compare_outputs, generate_case, quant_rows_ref,
                     int8_attention_layer_ref, int8_linear_ref, make_weights)
+from parity_util import no_worse_than_reference_rounding
 from tiktok_techjam_2026_track3_b200 import B200AttentionLayer, ops
 
 pytestmark = pytest.mark.gpu
 
-CASES = [(2, 512, 1024, 8, True), (1, 1000, 512, 4, False), (1, 4096, 4096, 32, True)]
+# (configuration 3 itself, B16 S4096 D4096 H32, is checked on seven seeds in test_gpu_configs.py)
+CASES = [(2, 512, 1024, 8, True), (1, 1000, 512, 4, False), (2, 1024, 2048, 16, True)]
 
 
-def _attn_fp32(qkv, H, causal):
+def _attn_fp32(qkv, H, causal, probs_dtype=None):
     B, S, D3 = qkv.shape
     D = D3 // 3
     hd = D // H
@@ -31,7 +33,10 @@ def _attn_fp32(qkv, H, causal):
     s = (q @ k.transpose(-1, -2)) * hd ** -0.5
     if causal:
         s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
-    return (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B, S, D)
+    p = torch.softmax(s, -1)
+    if probs_dtype is not None:
+        p = p.to(probs_dtype).float()
+    return (p @ v).transpose(1, 2).reshape(B, S, D)
 
 
 @pytest.mark.parametrize("B,S,D,H,causal", CASES)
@@ -65,9 +70,11 @@ def test_int8_layer_stagewise(B, S, D, H, causal):
     assert torch.equal(w8, wq8_ref) and torch.equal(s8, sq_ref)
     qkv_ref = int8_linear_ref(x.view(T, D).float(), wq8_ref, sq_ref, bqkv).to(torch.bfloat16)
     assert torch.equal(qkv.view(T, 3 * D), qkv_ref)
-    # 2. attention stage against fp32 on the same qkv (bf16 probabilities: abs 1e-2)
-    rep = compare_outputs(_attn_fp32(qkv, H, causal), ctx.float(), atol=1e-2)
-    assert rep.passed, f"attention stage: {rep}"
+    # 2. attention stage against fp32 on the same qkv, no worse than the reference's
+    #    own bf16 probabilities (torch_transformer_benchmark.py:111)
+    no_worse_than_reference_rounding(_attn_fp32(qkv, H, causal), ctx.float(),
+                                     _attn_fp32(qkv, H, causal, torch.bfloat16).to(torch.bfloat16).float(),
+                                     f"int8 B{B} S{S} D{D} attention stage")
     # 3. out-proj stage given our ctx: bit-exact against the recipe + residual
     wo8_ref, so_ref = quant_weight_ref(wb.wo)
     out_ref = (x.view(T, D).float() + int8_linear_ref(ctx.view(T, D).float(), wo8_ref, so_ref, wb.bo))

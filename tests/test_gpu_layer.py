@@ -31,8 +31,6 @@ def _rounded(w: LayerWeights, dtype):
 @pytest.mark.parametrize("name", FIXTURES)
 def test_layer_on_golden_inputs(golden_dir, dt, name):
     fx = torch.load(golden_dir / f"attn_{name}.pt", weights_only=False)
-    if fx["d_model"] // fx["heads"] not in (64, 128):
-        pytest.skip("head_dim outside the kernel set")
     w = LayerWeights.from_state_dict(fx["state_dict"])
     dtype = DT[dt]
     x = fx["x"].to(dtype)
@@ -125,5 +123,7 @@ def test_unsupported_inputs_raise():
         layer(torch.randn(1, 8, 256, device="cuda"), None, True)   # fp32 input
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         B200AttentionLayer(256, 4).half()(torch.randn(1, 8, 256).half(), None, True)
-    with pytest.raises(RuntimeError, match="head_dim"):
-        B200AttentionLayer(192, 2).cuda().half()(torch.randn(1, 8, 192, device="cuda").half())
+    with pytest.raises(RuntimeError, match="head_dim"):   # head_dim 12: not a multiple of 8
+        B200AttentionLayer(96, 8).cuda().half()(torch.randn(1, 8, 96, device="cuda").half())
+    with pytest.raises(RuntimeError, match="head_dim"):   # head_dim 512 > 256
+        B200AttentionLayer(512, 1).cuda().half()(torch.randn(1, 8, 512, device="cuda").half())

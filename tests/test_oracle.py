@@ -8,9 +8,10 @@ Project/kernels/k008_int8_gemm.py unmodified.
 import pytest
 import torch
 
-from oracle import (LayerWeights, attention_layer_ref, attention_layer_streamed_ref,
-                    compare_outputs, generate_case, int8_linear_ref, int_gemm_ref,
-                    quant_rows_ref, quant_weight_ref, split_heads, streamed_attention_ref)
+from oracle import (LayerWeights, attention_layer_ref, attention_layer_rows_ref,
+                    attention_layer_streamed_ref, compare_outputs, generate_case, int8_linear_ref,
+                    int_gemm_ref, make_weights, quant_rows_ref, quant_weight_ref, split_heads,
+                    streamed_attention_ref)
 
 ATTN_FIXTURES = ["cfg1_noncausal", "cfg1_causal", "padded_causal", "ragged_hd128", "tiny_s1"]
 
@@ -141,3 +142,84 @@ def test_block_oracle_matches_reference_model(golden_dir):
     with torch.inference_mode():
         out = model(fx["x"], fx["mask"])
     torch.testing.assert_close(out, fx["out"], rtol=1e-5, atol=1e-5)
+
+
+def _streamed_model(model):
+    """The model with every block's attention evaluated by the streamed checker,
+    per (batch, head), 512-key chunks (no S x S table): the substitution the
+    reference makes to check sequences whose dense scores do not fit
+    (Project/tools/shape14_eval.py:201-254)."""
+    import types
+
+    def fwd(self, x, valid_token_mask=None, causal=False, in_dtype=False):
+        B, S, D = x.shape
+        H = self.num_heads
+        q, k, v = (split_heads(torch.nn.functional.linear(x, m.weight, m.bias), H)
+                   for m in (self.q_proj, self.k_proj, self.v_proj))
+        ctx = torch.empty_like(q)
+        for b in range(B):
+            km = None if valid_token_mask is None else valid_token_mask[b]
+            for h in range(H):
+                ctx[b, h] = streamed_attention_ref(q[b, h], k[b, h], v[b, h], (D // H) ** -0.5, causal,
+                                                   key_mask=km, k_chunk=512)
+        out = torch.nn.functional.linear(ctx.transpose(1, 2).reshape(B, S, D), self.out_proj.weight,
+                                         self.out_proj.bias)
+        if valid_token_mask is not None:
+            out = out.masked_fill(~valid_token_mask[..., None], 0)
+        return out
+
+    for layer in model.layers:
+        layer.attention.forward = types.MethodType(fwd, layer.attention)
+    return model
+
+
+@pytest.mark.parametrize("seq,batch", [(1024, 2), (2048, 2), (4096, 1)])
+def test_streamed_checker_gate_whole_model(seq, batch):
+    """The reference's own gate for its long-context checker
+    (Project/tools/shape14_eval.py:279-316): the whole model (d_model 1024,
+    16 heads, ffn 1024, 2 layers, causal) with streamed attention against the
+    dense model, S in {1024, 2048, 4096}, three seeds each, max |diff| < 1e-3 in
+    fp32."""
+    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef
+    cfg = TransformerConfigRef(batch_size=batch, seq_len=seq, d_model=1024, num_heads=16, ffn_dim=1024,
+                               num_layers=2, causal=True)
+    torch.manual_seed(seq)
+    dense = BaselineTransformerRef(cfg).eval()
+    streamed = _streamed_model(BaselineTransformerRef(cfg).eval())
+    streamed.load_state_dict(dense.state_dict())
+    for seed in (1234, 1235, 1236):
+        x, mask = generate_case(batch, seq, 1024, seed)
+        with torch.inference_mode():
+            err = (streamed(x, mask) - dense(x, mask)).abs().max().item()
+        assert err < 1e-3, (seq, seed, err)
+
+
+def test_rows_ref_matches_dense_layer_and_rounding_points():
+    """attention_layer_rows_ref against the dense oracle (fp32), and its 16-bit
+    variant against a dense restatement that rounds at the same points."""
+    B, S, D, H = 2, 300, 256, 4
+    x, mask = generate_case(B, S, D, 11, padding_ratio=0.3)
+    x = x.to(torch.bfloat16).float()
+    w = make_weights(D, 11).to(dtype=torch.bfloat16).to(dtype=torch.float32)
+    rows = torch.tensor([0, 1, 2, 77, 150, 255, 299])
+    for causal in (True, False):
+        got32, got16 = attention_layer_rows_ref(x, w, H, causal, [0, 1], rows,
+                                                store_dtypes=(None, torch.bfloat16),
+                                                valid_token_mask=mask, k_chunk=64)
+        dense = attention_layer_ref(x, w, H, mask, causal)
+        torch.testing.assert_close(got32, dense[:, rows], rtol=1e-5, atol=1e-5)
+
+        def r(t):
+            return t.to(torch.bfloat16).float()
+        q, k, v = (r(split_heads(torch.nn.functional.linear(x, a, b), H))
+                   for a, b in ((w.wq, w.bq), (w.wk, w.bk), (w.wv, w.bv)))
+        sc = q @ k.transpose(-1, -2) * (D // H) ** -0.5
+        if causal:
+            sc = sc.masked_fill(torch.ones(S, S, dtype=torch.bool).triu(1), float("-inf"))
+        sc = sc.masked_fill(~mask[:, None, None, :], float("-inf"))
+        ctx = r(r(torch.softmax(sc, -1)) @ v).transpose(1, 2).reshape(B, S, D)
+        o = r(torch.nn.functional.linear(ctx, w.wo, w.bo)).masked_fill(~mask[..., None], 0)
+        ref16 = r(x + o)
+        torch.testing.assert_close(got16, ref16[:, rows], rtol=0, atol=2 ** -7)
+        # almost every element is the identical 16-bit value (accumulation order aside)
+        assert float((got16 == ref16[:, rows]).float().mean()) > 0.97

@@ -102,3 +102,48 @@ def test_gloo_batch_and_head_partitions_match_unpartitioned():
     ref = attention_layer_ref(x, make_weights(D, 5), H, mask, True)
     torch.testing.assert_close(res["batch"], ref, rtol=1e-5, atol=1e-5)
     torch.testing.assert_close(res["heads"], ref, rtol=1e-5, atol=1e-5)
+
+
+def _worker_reload_and_subgroup(rank, world, port, path):
+    """Heads mode must pick up new weights loaded between two forwards, and both
+    partitions must address their peers correctly inside a subgroup whose ranks
+    differ from the global ranks (global ranks 1 and 2 of a 3-rank world)."""
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    B, S, D, H = 3, 40, 128, 4
+    x, mask = generate_case(B, S, D, 78, padding_ratio=0.3)
+    results = {}
+    sub = dist.new_group([1, 2])
+    if rank in (1, 2):
+        layer = B200AttentionLayer(D, H)
+        layer.load_state_dict(make_weights(D, 5).state_dict())
+        sh = ShardedAttention(layer, "heads", group=sub, backend=OracleBackend())
+        first = sh(x, mask, True)
+        layer.load_state_dict(make_weights(D, 6).state_dict())   # new weights, same module
+        second = sh(x, mask, True)
+        gr = dist.get_rank(sub)
+        r0, r1 = shard_range(B, 2, gr)
+        shb = ShardedAttention(layer, "batch", group=sub, backend=OracleBackend())
+        out_b = shb(x[r0:r1], mask[r0:r1], True, gather=True, global_batch=B)
+        if gr == 0:
+            results = {"first": first, "second": second, "batch": out_b}
+        else:
+            assert first is None and second is None and out_b is None
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 1:
+        torch.save(results, path)
+
+
+def test_gloo_heads_reload_weights_and_subgroup_ranks():
+    world = 3
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "res.pt")
+        mp.spawn(_worker_reload_and_subgroup, args=(world, _free_port(), path), nprocs=world, join=True)
+        res = torch.load(path)
+    B, S, D, H = 3, 40, 128, 4
+    x, mask = generate_case(B, S, D, 78, padding_ratio=0.3)
+    ref1 = attention_layer_ref(x, make_weights(D, 5), H, mask, True)
+    ref2 = attention_layer_ref(x, make_weights(D, 6), H, mask, True)
+    torch.testing.assert_close(res["first"], ref1, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(res["second"], ref2, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(res["batch"], ref2, rtol=1e-5, atol=1e-5)

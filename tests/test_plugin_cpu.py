@@ -23,3 +23,24 @@ def test_build_keeps_reference_state_dict(golden_dir):
     attn = plugin.attention_sublayer(model.layers[0])
     assert attn.q_proj is model.layers[0].attention.q_proj
     assert list(model.state_dict().keys()) == list(ref.state_dict().keys())
+
+
+def test_official_shapes_table_matches_reference_manifest():
+    """config.OFFICIAL_SHAPES restates the reference's Project/shapes.json (read
+    here only when the reference checkout is present; it never travels)."""
+    import json
+    from pathlib import Path
+
+    import pytest
+
+    from tiktok_techjam_2026_track3_b200.config import OFFICIAL_SHAPES
+    manifest = Path("/root/reference/Project/shapes.json")
+    if not manifest.exists():
+        pytest.skip("reference checkout not present")
+    shapes = json.loads(manifest.read_text())["shapes"]
+    assert sorted(OFFICIAL_SHAPES) == sorted(s["id"] for s in shapes)
+    for s in shapes:
+        m = OFFICIAL_SHAPES[s["id"]]
+        assert (m.batch, m.d_model, m.num_heads, m.seq_len, m.num_layers, m.ffn_dim, m.causal) == (
+            s["batch_size"], s["d_model"], s["num_heads"], s["seq_len"], s["num_layers"], s["ffn_dim"],
+            s["causal"])

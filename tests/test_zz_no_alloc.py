@@ -67,6 +67,51 @@ def test_noalloc_matches_regular_entry_point_twice(B, S, D, H, causal, padded):
         print(f"call {call}: {rep}; bit-identical={torch.equal(out_regular, out_noalloc)}")
 
 
+def test_later_calls_map_no_more_device_memory():
+    """The array is mapped when the library's code first reaches the device (the
+    first call at the latest); after that a call must not change the device's free
+    memory, which is what a caller that reserved the rest of memory relies on."""
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    B, S, D, H = 2, 512, 512, 8
+    layer = B200AttentionLayer(D, H)
+    layer.load_state_dict(make_weights(D, 7).state_dict())
+    layer = layer.to(device=dev, dtype=torch.float16).eval()
+    pk = layer.packed_weights()
+    x = generate_case(B, S, D, 7, dtype=torch.float16)[0].to(dev)
+    out = torch.empty_like(x)
+    a = _args(x, pk, out, B, S, D, H, True, None, x, None)
+    assert lib.ttj_attn_layer_fwd_noalloc(C.byref(a), stream) == 0, lib.ttj_last_error()
+    torch.cuda.synchronize(dev)
+    free_after_first = torch.cuda.mem_get_info(dev)[0]
+    first = out.clone()
+    for _ in range(3):
+        assert lib.ttj_attn_layer_fwd_noalloc(C.byref(a), stream) == 0, lib.ttj_last_error()
+    torch.cuda.synchronize(dev)
+    assert torch.cuda.mem_get_info(dev)[0] == free_after_first
+    assert torch.equal(out, first)
+    ops.check_device_status(dev)
+
+
+def test_noalloc_rejects_unsupported_shapes_before_launching():
+    """Unsupported head_dim / dtype are rejected by the same checks as the regular
+    entry point, before any kernel is launched (the output stays untouched)."""
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    D, H = 512, 1   # head_dim 512 > 256
+    x = torch.zeros(1, 8, D, dtype=torch.float16, device=dev)
+    pk = tuple(torch.zeros(n, dtype=torch.float16, device=dev) for n in (3 * D * D, 3 * D, D * D, D))
+    out = torch.full_like(x, 7.0)
+    a = _args(x, pk, out, 1, 8, D, H, True)
+    rc = lib.ttj_attn_layer_fwd_noalloc(C.byref(a), torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == -2 and b"head_dim" in lib.ttj_last_error()
+    a.dtype = 7
+    assert lib.ttj_attn_layer_fwd_noalloc(C.byref(a), torch.cuda.current_stream(dev).cuda_stream) == -1
+    torch.cuda.synchronize(dev)
+    assert bool((out == 7.0).all())
+
+
 def test_noalloc_rejects_layers_beyond_its_scratch():
     lib = _lib.load()
     dev = torch.device("cuda", 0)

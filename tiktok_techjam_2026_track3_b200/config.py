@@ -14,7 +14,7 @@ from typing import Dict, Optional
 
 import torch
 
-__all__ = ["LayerConfig", "PRESETS", "DTYPES", "attention_flops"]
+__all__ = ["LayerConfig", "PRESETS", "DTYPES", "attention_flops", "ModelShape", "OFFICIAL_SHAPES"]
 
 DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
 
@@ -50,10 +50,10 @@ class LayerConfig:
             raise ValueError("batch, seq_len, d_model and num_heads must be positive")
         if self.d_model % self.num_heads != 0:
             raise ValueError(f"d_model ({self.d_model}) must be divisible by num_heads ({self.num_heads})")
-        if self.head_dim not in (64, 128):
-            raise ValueError("head_dim must be 64 or 128 for the sm_100a kernels")
-        if self.d_model % 64 != 0:
-            raise ValueError("d_model must be a multiple of 64")
+        if self.head_dim % 8 != 0 or self.head_dim > 256:
+            raise ValueError("head_dim must be a multiple of 8 and at most 256 for the sm_100a kernels")
+        if self.d_model % 32 != 0:
+            raise ValueError("d_model must be a multiple of 32")
         if self.dtype not in DTYPES:
             raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
         if self.quant not in (None, "int8"):
@@ -88,4 +88,43 @@ PRESETS: Dict[int, LayerConfig] = {
                    dtype="bfloat16"),
     5: LayerConfig("cfg5_bf16_b1_s262144_d4096_h32_causal", 1, 262144, 4096, 32, causal=True,
                    dtype="bfloat16", shard="heads"),
+}
+
+
+@dataclass(frozen=True)
+class ModelShape:
+    """One whole-model benchmark shape: the CLI dials of the reference's
+    torch_transformer_benchmark.py (--batch-size, --d-model, --heads, --seq-len,
+    --layers, --ffn-dim; every official shape passes --causal)."""
+    batch: int
+    d_model: int
+    num_heads: int
+    seq_len: int
+    num_layers: int
+    ffn_dim: int
+    causal: bool = True
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.num_heads
+
+
+# The 14 official test shapes of the reference (Project/shapes.json, ids 1-14).
+# head_dim spans 8 (ids 7, 11), 32 (ids 1-6, 12, 13), 64 (ids 10, 14),
+# 128 (id 9) and 256 (id 8).  Id 14 cannot run through the dense reference.
+OFFICIAL_SHAPES: Dict[int, ModelShape] = {
+    1: ModelShape(64, 128, 4, 128, 4, 128),
+    2: ModelShape(1, 128, 4, 128, 4, 128),
+    3: ModelShape(4, 128, 4, 128, 4, 128),
+    4: ModelShape(16, 128, 4, 128, 4, 128),
+    5: ModelShape(128, 128, 4, 128, 4, 128),
+    6: ModelShape(10000, 128, 4, 128, 4, 128),
+    7: ModelShape(64, 32, 4, 128, 4, 32),
+    8: ModelShape(64, 1024, 4, 128, 4, 1024),
+    9: ModelShape(64, 128, 1, 128, 4, 128),
+    10: ModelShape(64, 128, 2, 128, 4, 128),
+    11: ModelShape(64, 128, 16, 128, 4, 128),
+    12: ModelShape(64, 128, 4, 32, 4, 128),
+    13: ModelShape(64, 128, 4, 1024, 4, 128),
+    14: ModelShape(32, 1024, 16, 100000, 2, 1024),
 }

@@ -77,10 +77,7 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 
 }  // namespace ttj
 
-using ttj::aligned16;
-using ttj::fail;
-
-namespace {
+namespace ttj {
 
 int check_dtype(int dtype) {
   return (dtype == TTJ_F16 || dtype == TTJ_BF16) ? TTJ_OK
@@ -90,18 +87,38 @@ int check_dtype(int dtype) {
 int check_layer_shape(int64_t batch, int64_t seq_len, int64_t d_model, int64_t num_heads) {
   if (batch <= 0 || seq_len <= 0 || d_model <= 0 || num_heads <= 0)
     return fail(TTJ_ERR_INVALID_ARG, "batch, seq_len, d_model and num_heads must be positive");
+  // Each factor is bounded before any product is formed, so none can overflow.
+  if (batch >= kMaxBatch || seq_len > kMaxSeqLen || d_model > kMaxDModel)
+    return fail(TTJ_ERR_UNSUPPORTED, "batch, seq_len or d_model above the supported maximum");
   if (d_model % num_heads != 0)
     return fail(TTJ_ERR_INVALID_ARG, "d_model must be divisible by num_heads");
   const int64_t hd = d_model / num_heads;
-  if (hd != 64 && hd != 128) return fail(TTJ_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
-  if (d_model % 64 != 0) return fail(TTJ_ERR_UNSUPPORTED, "d_model must be a multiple of 64");
-  if (seq_len > (int64_t)65535 * 128) return fail(TTJ_ERR_UNSUPPORTED, "seq_len above 8388480");
-  if (batch * seq_len * 3 * d_model >= ((int64_t)1 << 46))
+  if (hd % 8 != 0 || hd > 256)
+    return fail(TTJ_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  if (d_model % 32 != 0) return fail(TTJ_ERR_UNSUPPORTED, "d_model must be a multiple of 32");
+  const int64_t tokens = batch * seq_len;  // < 2^31 * 2^23: no overflow
+  if (tokens > (((int64_t)1 << 46) - 1) / (3 * d_model))
     return fail(TTJ_ERR_UNSUPPORTED, "tensor too large");
   return TTJ_OK;
 }
 
+}  // namespace ttj
+
+using ttj::aligned16;
+using ttj::check_dtype;
+using ttj::check_layer_shape;
+using ttj::fail;
+
+namespace {
+
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Workspace sizes are only meaningful for shapes the layer accepts; outside the
+// per-factor limits the byte counts could overflow, so they report 0.
+bool size_args_ok(int64_t batch, int64_t seq_len, int64_t d_model) {
+  return batch > 0 && seq_len > 0 && d_model > 0 && batch < ttj::kMaxBatch &&
+         seq_len <= ttj::kMaxSeqLen && d_model <= ttj::kMaxDModel;
+}
 
 }  // namespace
 
@@ -240,7 +257,7 @@ int ttj_out_proj_residual_fwd(const void* ctx, const void* w_o, const void* b_o,
 
 size_t ttj_attn_layer_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model, int dtype) {
   (void)dtype;
-  if (batch <= 0 || seq_len <= 0 || d_model <= 0) return 0;
+  if (!size_args_ok(batch, seq_len, d_model)) return 0;
   const size_t t = (size_t)batch * (size_t)seq_len;
   return round_up(t * 3 * d_model * 2, 256) + round_up(t * d_model * 2, 256);
 }
@@ -330,7 +347,7 @@ int ttj_int8_linear_fwd(const int8_t* a, const float* s_a, const int8_t* w, cons
 
 size_t ttj_int8_attn_layer_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model, int dtype) {
   (void)dtype;
-  if (batch <= 0 || seq_len <= 0 || d_model <= 0) return 0;
+  if (!size_args_ok(batch, seq_len, d_model)) return 0;
   const size_t t = (size_t)batch * (size_t)seq_len, d = (size_t)d_model;
   return round_up(t * d, 256)            /* int8 activations (x, then ctx) */
          + round_up(t * 4, 256)          /* per-token scales */
@@ -413,7 +430,7 @@ int ttj_linear_gelu_fwd(const void* x, const void* w, const void* bias, void* y,
 size_t ttj_block_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model, int64_t ffn_dim,
                                 int dtype) {
   (void)dtype;
-  if (batch <= 0 || seq_len <= 0 || d_model <= 0 || ffn_dim <= 0) return 0;
+  if (!size_args_ok(batch, seq_len, d_model) || ffn_dim <= 0 || ffn_dim >= (1ll << 31)) return 0;
   const size_t t = (size_t)batch * (size_t)seq_len, d = (size_t)d_model, f = (size_t)ffn_dim;
   const size_t wide = 3 * d > f ? 3 * d : f;
   return round_up(t * d * 2, 256)        /* normalised input (norm1, then norm2) */
@@ -428,7 +445,8 @@ int ttj_transformer_block_fwd(const ttj_block_args* a, ttj_stream_t stream) {
   if (int rc = check_layer_shape(a->batch, a->seq_len, a->d_model, a->num_heads)) return rc;
   TTJ_CHECK_ARG(a->ffn_dim > 0 && a->ffn_dim % 32 == 0 && a->ffn_dim < (1ll << 31), TTJ_ERR_UNSUPPORTED,
                 "ffn_dim must be a positive multiple of 32");
-  TTJ_CHECK_ARG(a->batch * a->seq_len * a->ffn_dim < (1ll << 46), TTJ_ERR_UNSUPPORTED, "tensor too large");
+  TTJ_CHECK_ARG(a->batch * a->seq_len <= (((int64_t)1 << 46) - 1) / a->ffn_dim, TTJ_ERR_UNSUPPORTED,
+                "tensor too large");
   TTJ_CHECK_ARG(a->x && a->ln1_w && a->ln1_b && a->w_qkv && a->b_qkv && a->w_o && a->b_o && a->ln2_w &&
                     a->ln2_b && a->w_in && a->b_in && a->w_out && a->b_out && a->out,
                 TTJ_ERR_INVALID_ARG, "x, parameters and out must be non-NULL");

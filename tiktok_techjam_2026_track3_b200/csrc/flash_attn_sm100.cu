@@ -1,13 +1,18 @@
 // Flash-attention forward for sm_100a (persistent, two query tiles per work item).
 //
 // Q, K and V are read straight from the packed projection buffer qkv[B,S,3D]
-// through one 3-D TMA descriptor (dims 3D x S x B, box 64 x 128 x 1, 128-byte
-// swizzle): the reference's head split (.view/.transpose/.contiguous) becomes a
-// coordinate choice, and rows past S arrive as zeros.
+// through one 4-D TMA descriptor (dims head_dim x 3H x S x B, box 64 x 1 x 128
+// x 1, 128-byte swizzle): the reference's head split (.view/.transpose/
+// .contiguous) becomes a coordinate choice, rows past S arrive as zeros, and so
+// do the columns past head_dim.  The kernel is compiled for padded head sizes
+// HD = 64, 128 and 256 and runs any head_dim that is a multiple of 8 up to HD:
+// the zero columns add nothing to Q K^T and give zero columns of P V, which the
+// context store (a 4-D map of the same shape) clips away.
 //
 // Work item = (batch, head, 256 consecutive queries) = two 128-row query tiles
-// A and B that share every K/V tile.  One CTA per SM loops over work items,
-// heaviest (longest causal key range) first.
+// A and B that share every K/V tile (HD 256: one 128-row tile, tensor memory
+// holds one S and one 256-column O per tile).  One CTA per SM loops over work
+// items, heaviest (longest causal key range) first.
 //
 // Roles (384 threads = 12 warps = 3 warpgroups):
 //   warp 0       TMA: K_j / V_j tiles into KV_STAGES-deep rings, item after item
@@ -37,6 +42,8 @@
 //   order per tile is PV_t(j-1), QK_t(j), commit s_full_t.  tcgen05.commit
 //   arrives only when every earlier MMA of the issuing thread has completed,
 //   so "S_t(j) is ready" also means P_t(j-1) was consumed and O_t is stable.
+// head_dim 256: the same schedule for tile A alone, S_A [0,128) O_A [256,512),
+//   one K and one V stage (64 KB each).
 #include "sm100_ptx.cuh"
 #include "ttj_internal.h"
 
@@ -60,8 +67,9 @@ constexpr int64_t kHeadMajorKvBytes = int64_t(96) << 20;
 struct AttnParams {
   void* ctx;
   const uint8_t* key_mask;
-  int B, S, H, D;
-  int num_pairs;     // ceil(S / 256)
+  int B, S, H;
+  int hd;            // real head_dim (<= the kernel's padded HD)
+  int num_pairs;     // ceil(S / (128 * tiles per item))
   int num_items;     // B * H * num_pairs
   int head_major;    // item order: 1 = a head's pairs consecutive, 0 = pair index outermost
   float scale_log2;  // head_dim^-0.5 * log2(e)
@@ -70,21 +78,23 @@ struct AttnParams {
 
 template <int HD>
 struct AttnSmem {
+  static_assert(HD == 64 || HD == 128 || HD == 256, "padded head sizes");
+  static constexpr int kNT = HD == 256 ? 1 : 2;     // query tiles per work item
   static constexpr bool kSepP = HD == 64;           // separate P buffers in TMEM
-  static constexpr int kStages = HD == 64 ? 4 : 2;
+  static constexpr int kStages = HD == 64 ? 4 : (HD == 128 ? 2 : 1);
   static constexpr int kTileBytes = HD * 2 * 128;  // 128 rows x HD x 2 bytes
   // Q tiles: head_dim 64 double-buffers them (the next item's Q arrives while
-  // this item runs); head_dim 128 has no room.
+  // this item runs); the larger heads have no room.
   static constexpr int kQBufs = HD == 64 ? 2 : 1;
   static constexpr int kQOff = 0;                   // [kQBufs][Q_A, Q_B]
-  static constexpr int kKOff = 2 * kQBufs * kTileBytes;
+  static constexpr int kKOff = kNT * kQBufs * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   // The context rows leave through TMA stores from a 4 KB staging box per
-  // softmax warp (32 rows x 64 columns, 128-byte swizzle; head_dim 128 reuses
-  // it for its second 64 columns); measured: per-thread 16-byte row stores took
-  // 1-2.5K cycles per item end at head_dim 64, ~3.5K at head_dim 128.
+  // softmax warp (32 rows x 64 columns, 128-byte swizzle; larger heads reuse
+  // it for each further 64 columns); measured: per-thread 16-byte row stores
+  // took 1-2.5K cycles per item end at head_dim 64, ~3.5K at head_dim 128.
   static constexpr int kEpiOff = kVOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kEpiOff + 8 * 32 * 128;
+  static constexpr int kBarOff = kEpiOff + 4 * kNT * 32 * 128;
   static constexpr int kTotal = 1024 + kBarOff + 512;
   static_assert(kTotal <= 232448, "shared memory budget");
   // TMEM columns
@@ -131,7 +141,7 @@ __device__ __forceinline__ int item_of(int k) {
   return k * (int)gridDim.x + ((k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
 }
 
-// Decode work item -> (b, h, pair).  Causal pairs come in decreasing pair
+// Decode work item -> (b, h, pair); a "pair" is the item's group of query tiles.  Causal pairs come in decreasing pair
 // index (longest key range first).  Pair-major order (the pair index
 // outermost) keeps the whole grid on items of equal length, which balances
 // short sequences best.  Head-major order (a head's pairs consecutive) is used
@@ -159,11 +169,11 @@ __device__ __forceinline__ Item decode_item(int item, const AttnParams& p) {
   return it;
 }
 
-// Number of key tiles tile `t` (0 = A, 1 = B) of a pair attends to.
-template <bool CAUSAL>
+// Number of key tiles tile `t` (0 = A, 1 = B) of a pair attends to (NT tiles per pair).
+template <bool CAUSAL, int NT>
 __device__ __forceinline__ int kv_tiles(int pair, int t, int S) {
   const int total = (S + kBN - 1) / kBN;
-  return CAUSAL ? min(2 * pair + 1 + t, total) : total;
+  return CAUSAL ? min(NT * pair + 1 + t, total) : total;
 }
 
 template <typename T, int HD, bool CAUSAL>
@@ -172,6 +182,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
                  const AttnParams p) {
   using L = AttnSmem<HD>;
   constexpr int ST = L::kStages;
+  constexpr int NT = L::kNT;
   constexpr bool kSepP = L::kSepP;
   constexpr int kChunks = HD / 64;
   constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -266,9 +277,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         const int item = item_of(k);
         if (item >= p.num_items) break;
         const Item it = decode_item<CAUSAL>(item, p);
-        const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
-        const int n_kv = kv_tiles<CAUSAL>(it.pair, 1, p.S);
-        const int xk = p.D + it.h * HD, xv = 2 * p.D + it.h * HD;
+        const int n_a = kv_tiles<CAUSAL, NT>(it.pair, 0, p.S);
+        const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, 1, p.S);
+        const int yk = p.H + it.h, yv = 2 * p.H + it.h;  // head index of K / V in the 3H axis
         for (int j = 0; j < n_kv; ++j, ++kv) {
           const int st = kv % ST;
           // bit t: tile t releases this key tile (with P over S one thread issues
@@ -277,11 +288,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           if (!reclaim(k_empty, kpend, kph, st, users)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
           for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], xk + 64 * c, j * kBN, it.b);
+            tma_load_4d(sK + st * L::kTileBytes + c * kChunkBytes, &tm, &k_full[st], 64 * c, yk, j * kBN, it.b);
           if (!reclaim(v_empty, vpend, vph, st, users)) { ok = false; break; }
           mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
           for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], xv + 64 * c, j * kBN, it.b);
+            tma_load_4d(sV + st * L::kTileBytes + c * kChunkBytes, &tm, &v_full[st], 64 * c, yv, j * kBN, it.b);
         }
       }
     } else if (warp == 2 && lane == 0) {
@@ -291,22 +302,22 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         if (item >= p.num_items) break;
         const Item it = decode_item<CAUSAL>(item, p);
         bool ok = true;
-        for (int t = 0; t < 2 && ok; ++t) {
+        for (int t = 0; t < NT && ok; ++t) {
           const int qb = k % L::kQBufs;
           const uint32_t qph = (k / L::kQBufs) & 1;
           ok = mbar_wait(&q_empty[qb * 2 + t], qph ^ 1u, p.status, kDevTimeoutSmemEmpty, abort_flag);
           if (!ok) break;
           mbar_arrive_expect_tx(&q_full[qb * 2 + t], L::kTileBytes);
           for (int c = 0; c < kChunks; ++c)
-            tma_load_3d(sQ + (qb * 2 + t) * L::kTileBytes + c * kChunkBytes, &tm, &q_full[qb * 2 + t], it.h * HD + 64 * c,
-                        it.pair * 2 * kBM + t * kBM, it.b);
+            tma_load_4d(sQ + (qb * NT + t) * L::kTileBytes + c * kChunkBytes, &tm, &q_full[qb * 2 + t], 64 * c, it.h,
+                        it.pair * NT * kBM + t * kBM, it.b);
         }
         if (!ok) break;
       }
     } else if (lane == 0 && (warp == 1 || (kSepP && warp == 3))) {
       // ------------------------------------------------------------ MMA issue
       auto qk = [&](int t, int st, int qb) {
-        const uint32_t q_addr = smem_u32(sQ + (qb * 2 + t) * L::kTileBytes);
+        const uint32_t q_addr = smem_u32(sQ + (qb * NT + t) * L::kTileBytes);
         const uint32_t k_addr = smem_u32(sK + st * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -339,8 +350,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           const int item = item_of(qk_k);
           if (item >= p.num_items) return false;
           const Item it = decode_item<CAUSAL>(item, p);
-          qk_n = kv_tiles<CAUSAL>(it.pair, t, p.S);
-          qk_nb = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+          qk_n = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
+          qk_nb = kv_tiles<CAUSAL, NT>(it.pair, 1, p.S);
           return true;
         };
         bool qk_live = qk_open();
@@ -378,8 +389,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           const int item = item_of(k);
           if (item >= p.num_items) break;
           const Item it = decode_item<CAUSAL>(item, p);
-          const int n = kv_tiles<CAUSAL>(it.pair, t, p.S);
-          const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);
+          const int n = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
+          const int n_b = kv_tiles<CAUSAL, NT>(it.pair, 1, p.S);
           for (int j = 0; j < n; ++j) {
             // S_t(j+1), or the next item's S_t(0) (its Q is double-buffered, so
             // normally already loaded), then this key tile's P.V.  Issuing the
@@ -406,7 +417,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         // P over S: one thread issues both tiles, PV_A(j) QK_A(j+1) PV_B(j)
         // QK_B(j+1) (measured faster here than one thread per tile: each tile's
         // next S waits for its own P.V, and the fixed interleave keeps the two
-        // tiles' softmax steps half a step apart).
+        // tiles' softmax steps half a step apart).  With one tile per item
+        // (head_dim 256) only the tile-A half of each step is issued; the
+        // stage releases still go through tile B's barriers, which is where
+        // the producer waits for them.
         int kv = 0;
         uint32_t pf_phase[2] = {0u, 0u};
         bool ok = true;
@@ -417,10 +431,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           const int item = item_of(k);
           if (item >= p.num_items) break;
           const Item it = decode_item<CAUSAL>(item, p);
-          const int n_a = kv_tiles<CAUSAL>(it.pair, 0, p.S);
-          const int n_b = kv_tiles<CAUSAL>(it.pair, 1, p.S);  // n_b >= n_a
+          const int n_a = kv_tiles<CAUSAL, NT>(it.pair, 0, p.S);
+          // key tiles of the item's last tile (n_b >= n_a)
+          const int n_b = kv_tiles<CAUSAL, NT>(it.pair, NT - 1, p.S);
           if (!mbar_wait(&q_full[0], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
-          if (!mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
+          if (NT == 2 && !mbar_wait(&q_full[1], k & 1, p.status, kDevTimeoutTmaFull, abort_flag)) break;
           const int kv0 = kv;
           {
             const int st = kv0 % ST;
@@ -429,9 +444,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
             qk(0, st, 0);
             umma_commit(&s_full[0]);
             if (n_a == 1) umma_commit(&q_empty[0]);
-            qk(1, st, 0);
-            umma_commit(&s_full[1]);
-            if (n_b == 1) umma_commit(&q_empty[1]);
+            if constexpr (NT == 2) {
+              qk(1, st, 0);
+              umma_commit(&s_full[1]);
+              if (n_b == 1) umma_commit(&q_empty[1]);
+            }
             release(k_empty, st);
           }
           for (int j = 0; j < n_b; ++j) {
@@ -442,31 +459,35 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
             const bool next_b = j + 1 < n_b;
             if (next_b && !mbar_wait(&k_full[st_n], ph_n, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
             if (!mbar_wait(&v_full[st], ph, p.status, kDevTimeoutTmaFull, abort_flag)) { ok = false; break; }
-            if (j < n_a) {
-              if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-              pf_phase[0] ^= 1u;
-              tc_fence_after();
-              pv(0, st, j > 0);
-              if (j + 1 < n_a) {
-                qk(0, st_n, 0);
-                umma_commit(&s_full[0]);
-                if (j + 2 == n_a) umma_commit(&q_empty[0]);
-              } else {
-                umma_commit(&o_done[0]);
+            if constexpr (NT == 2) {
+              if (j < n_a) {
+                if (!mbar_wait(&p_full[0], pf_phase[0], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+                pf_phase[0] ^= 1u;
+                tc_fence_after();
+                pv(0, st, j > 0);
+                if (j + 1 < n_a) {
+                  qk(0, st_n, 0);
+                  umma_commit(&s_full[0]);
+                  if (j + 2 == n_a) umma_commit(&q_empty[0]);
+                } else {
+                  umma_commit(&o_done[0]);
+                }
               }
             }
-            if (!mbar_wait(&p_full[1], pf_phase[1], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-            pf_phase[1] ^= 1u;
+            // The item's last tile (tile B, or tile A alone with one tile per item).
+            constexpr int tl = NT - 1;
+            if (!mbar_wait(&p_full[tl], pf_phase[tl], p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+            pf_phase[tl] ^= 1u;
             tc_fence_after();
-            pv(1, st, j > 0);
+            pv(tl, st, j > 0);
             release(v_empty, st);
             if (next_b) {
-              qk(1, st_n, 0);
-              umma_commit(&s_full[1]);
+              qk(tl, st_n, 0);
+              umma_commit(&s_full[tl]);
               release(k_empty, st_n);
-              if (j + 2 == n_b) umma_commit(&q_empty[1]);
+              if (j + 2 == n_b) umma_commit(&q_empty[tl]);
             } else {
-              umma_commit(&o_done[1]);
+              umma_commit(&o_done[tl]);
             }
           }
           kv = kv0 + n_b;
@@ -479,6 +500,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
     setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax (tile A or B)
     const int t = warp >= 8 ? 1 : 0;
+    if (t < NT) {  // one tile per item: warps 8..11 have no work
     const int lg = warp & 3;             // TMEM lane quarter of this warp
     const int r = lg * 32 + lane;        // query row within the tile
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(lg * 32) << 16);
@@ -492,8 +514,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       const int item = item_of(k);
       if (item >= p.num_items) break;
       const Item it = decode_item<CAUSAL>(item, p);
-      const int n_kv = kv_tiles<CAUSAL>(it.pair, t, p.S);
-      const int q0 = it.pair * 2 * kBM + t * kBM;
+      const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
+      const int q0 = it.pair * NT * kBM + t * kBM;
       const int q_row = q0 + r;
       const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
       // Key-mask bytes of the current key tile (lane l: keys l, l+32, l+64,
@@ -654,6 +676,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       uint8_t* box = smem + L::kEpiOff + (warp - 4) * (32 * 128);
 #pragma unroll
       for (int hh = 0; hh < HD / 64; ++hh) {
+        if (64 * hh >= p.hd) break;  // only zero padding left (uniform)
         if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
         __syncwarp();
 #pragma unroll
@@ -674,7 +697,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&tm_ctx, box, it.h * HD + 64 * hh, q0 + lg * 32, it.b);  // rows >= S are clipped
+          // rows >= S and columns >= head_dim are clipped by the map
+          tma_store_4d(&tm_ctx, box, 64 * hh, it.h, q0 + lg * 32, it.b);
           bulk_commit_group();
         }
       }
@@ -682,6 +706,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       // p_full arrival, which follows these TMEM loads.
     }
     if (lane == 0) bulk_wait_group_all();  // context stores complete before exit
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -692,23 +717,26 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
 template <typename T, int HD, bool CAUSAL>
 int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   using L = AttnSmem<HD>;
-  const int64_t D = a.num_heads * a.head_dim;
+  constexpr int NT = L::kNT;
+  const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t hd = (uint64_t)a.head_dim, H = (uint64_t)a.num_heads, D = H * hd;
+  // qkv [B, S, 3D] seen as [B][S][3H][head_dim]: head h of q / k / v is index
+  // h / H + h / 2H + h of the 3H axis.  The box is 64 columns wide whatever
+  // head_dim is; columns past head_dim read as zeros.
   CUtensorMap tm;
-  const uint64_t dims[3] = {(uint64_t)(3 * D), (uint64_t)a.seq_len, (uint64_t)a.batch};
-  const uint64_t strides[2] = {(uint64_t)(3 * D * 2), (uint64_t)(a.seq_len * 3 * D * 2)};
-  const uint32_t box[3] = {64, 128, 1};
-  int rc = encode_tmap(&tm, std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                       3, a.qkv, dims, strides, box);
+  const uint64_t dims[4] = {hd, 3 * H, (uint64_t)a.seq_len, (uint64_t)a.batch};
+  const uint64_t strides[3] = {hd * 2, 3 * D * 2, (uint64_t)a.seq_len * 3 * D * 2};
+  const uint32_t box[4] = {64, 1, 128, 1};
+  int rc = encode_tmap(&tm, dt, 4, a.qkv, dims, strides, box);
   if (rc) return rc;
-  // ctx [B, S, D]: the epilogue's 32-row x 64-column boxes
+  // ctx [B, S, D] seen as [B][S][H][head_dim]: the epilogue's 32-row x 64-column
+  // boxes, clipped at head_dim and at S.
   CUtensorMap tm_ctx;
-  const uint64_t cdims[3] = {(uint64_t)D, (uint64_t)a.seq_len, (uint64_t)a.batch};
-  const uint64_t cstrides[2] = {(uint64_t)(D * 2), (uint64_t)(a.seq_len * D * 2)};
-  const uint32_t cbox[3] = {64, 32, 1};
-  rc = encode_tmap(&tm_ctx, std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                   3, a.ctx, cdims, cstrides, cbox);
+  const uint64_t cdims[4] = {hd, H, (uint64_t)a.seq_len, (uint64_t)a.batch};
+  const uint64_t cstrides[3] = {hd * 2, D * 2, (uint64_t)a.seq_len * D * 2};
+  const uint32_t cbox[4] = {64, 1, 32, 1};
+  rc = encode_tmap(&tm_ctx, dt, 4, a.ctx, cdims, cstrides, cbox);
   if (rc) return rc;
   AttnParams p;
   p.ctx = a.ctx;
@@ -716,14 +744,14 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   p.B = (int)a.batch;
   p.S = (int)a.seq_len;
   p.H = (int)a.num_heads;
-  p.D = (int)D;
-  p.num_pairs = (int)((a.seq_len + 2 * kBM - 1) / (2 * kBM));
+  p.hd = (int)a.head_dim;
+  p.num_pairs = (int)((a.seq_len + NT * kBM - 1) / (NT * kBM));
   const int64_t items = a.batch * a.num_heads * (int64_t)p.num_pairs;
   // K and V of every head (2 x S x head_dim x 2 bytes each) against ~3/4 of the 126 MB L2.
-  p.head_major = a.batch * a.num_heads * a.seq_len * HD * 4 > kHeadMajorKvBytes ? 1 : 0;
+  p.head_major = a.batch * a.num_heads * a.seq_len * a.head_dim * 4 > kHeadMajorKvBytes ? 1 : 0;
   if (items >= (int64_t)1 << 31) return fail(TTJ_ERR_UNSUPPORTED, "too many attention work items");
   p.num_items = (int)items;
-  p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
+  p.scale_log2 = (float)(1.0 / sqrt((double)a.head_dim) * 1.4426950408889634);
   p.status = a.status;
   auto kern = flash_fwd_kernel<T, HD, CAUSAL>;
   {
@@ -740,10 +768,17 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   return TTJ_OK;
 }
 
+// head_dim runs on the kernel of the next padded size: up to 64, up to 128, up to 256.
+template <typename T, int HD>
+int dispatch_causal(const AttnArgs& a, cudaStream_t stream) {
+  return a.causal ? launch_attn<T, HD, true>(a, stream) : launch_attn<T, HD, false>(a, stream);
+}
+
 template <typename T>
 int dispatch_hd(const AttnArgs& a, cudaStream_t stream) {
-  if (a.head_dim == 64) return a.causal ? launch_attn<T, 64, true>(a, stream) : launch_attn<T, 64, false>(a, stream);
-  return a.causal ? launch_attn<T, 128, true>(a, stream) : launch_attn<T, 128, false>(a, stream);
+  if (a.head_dim <= 64) return dispatch_causal<T, 64>(a, stream);
+  if (a.head_dim <= 128) return dispatch_causal<T, 128>(a, stream);
+  return dispatch_causal<T, 256>(a, stream);
 }
 
 }  // namespace

@@ -24,7 +24,13 @@
 //
 // Set-up: the device address of the array is looked up (cudaGetSymbolAddress)
 // the first time the entry point runs on a device, with that device current,
-// and cached.  Make that first call before any stream capture begins.
+// and cached.  Make that first call before any stream capture begins.  The
+// CUDA runtime loads a library's device code onto a device lazily (the default
+// module-loading mode), so that same first call is also when the 32 MiB array
+// is mapped on the device: it grows device memory by 32 MiB once, and fails
+// with TTJ_ERR_CUDA if the device has no 32 MiB left.  A caller that reserves
+// the rest of device memory up front should make its first call on each device
+// during start-up, before that reservation; later calls map nothing more.
 #include <cstdio>
 #include <mutex>
 
@@ -65,14 +71,15 @@ size_t round_up256(size_t v) { return (v + 255) / 256 * 256; }
 
 extern "C" int ttj_attn_layer_fwd_noalloc(const ttj_attn_layer_args* a, ttj_stream_t stream) {
   if (a == nullptr) return ttj::fail(TTJ_ERR_INVALID_ARG, "args is NULL");
+  // The same checks, in the same order, as ttj_attn_layer_fwd: a rejected call
+  // launches nothing.
+  if (int rc = ttj::check_dtype(a->dtype)) return rc;
+  if (int rc = ttj::check_layer_shape(a->batch, a->seq_len, a->d_model, a->num_heads)) return rc;
   if (a->x == nullptr || a->w_qkv == nullptr || a->b_qkv == nullptr || a->w_o == nullptr ||
       a->b_o == nullptr || a->out == nullptr)
     return ttj::fail(TTJ_ERR_INVALID_ARG, "x, weights, biases and out must be non-NULL");
   if (a->out == a->x || a->out == a->residual)
     return ttj::fail(TTJ_ERR_INVALID_ARG, "out must not alias x or residual");
-  if (a->batch <= 0 || a->seq_len <= 0 || a->d_model <= 0 || a->num_heads <= 0 ||
-      a->d_model % a->num_heads != 0)
-    return ttj::fail(TTJ_ERR_INVALID_ARG, "bad batch / seq_len / d_model / num_heads");
   const size_t need = ttj_attn_layer_workspace_size(a->batch, a->seq_len, a->d_model, a->dtype);
   if (need > kNoAllocScratchBytes) {
     char buf[200];

@@ -30,6 +30,17 @@ int fail(int code, const std::string& why);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Per-factor limits of the layer entry points, checked before any product of
+// sizes is formed.  kMaxSeqLen keeps every query-tile row coordinate of the
+// attention kernel below 2^23.
+constexpr int64_t kMaxBatch = (int64_t)1 << 31;
+constexpr int64_t kMaxSeqLen = (int64_t)65535 * 128;
+constexpr int64_t kMaxDModel = (int64_t)1 << 16;
+
+// Argument checks shared by every layer entry point (TTJ_OK or a ttj_status).
+int check_dtype(int dtype);
+int check_layer_shape(int64_t batch, int64_t seq_len, int64_t d_model, int64_t num_heads);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

@@ -90,19 +90,28 @@ class ShardedAttention:
             if H % self.world != 0:
                 raise ValueError(f"heads ({H}) must divide evenly over {self.world} ranks")
 
+    def _peer(self, r: int) -> int:
+        """Global rank of rank ``r`` of this partition's group (``P2POp`` takes
+        global ranks; the partition works in group ranks)."""
+        return r if self.group is None else dist.get_global_rank(self.group, r)
+
     # ---------------------------------------------------------------- heads
     def head_weights(self):
-        """This rank's slice of the packed projection: q, k and v rows of its heads."""
-        if self._head_pack is None:
-            w_qkv, b_qkv, w_o, b_o = self.layer.packed_weights()
+        """This rank's slice of the packed projection: q, k and v rows of its heads.
+
+        Cached on the packed weights it was cut from: the layer repacks them
+        (new tensors) after ``load_state_dict``, ``.to()`` or an in-place edit,
+        and the slice is then cut again."""
+        w_qkv, b_qkv, w_o, b_o = self.layer.packed_weights()
+        if self._head_pack is None or self._head_pack[0] is not w_qkv or self._head_pack[1] is not b_qkv:
             D = self.layer.d_model
             hd = self.layer.head_dim
             h0, h1 = shard_range(self.layer.num_heads, self.world, self.rank)
             rows = torch.cat([torch.arange(s * D + h0 * hd, s * D + h1 * hd) for s in range(3)])
             rows = rows.to(w_qkv.device)
-            self._head_pack = (w_qkv.index_select(0, rows).contiguous(),
-                               b_qkv.index_select(0, rows).contiguous(), h1 - h0, w_o, b_o)
-        return self._head_pack
+            self._head_pack = (w_qkv, b_qkv, (w_qkv.index_select(0, rows).contiguous(),
+                                              b_qkv.index_select(0, rows).contiguous(), h1 - h0, w_o, b_o))
+        return self._head_pack[2]
 
     def _forward_heads(self, x, mask, causal):
         B, S, D = x.shape
@@ -113,13 +122,13 @@ class ShardedAttention:
             chunks = torch.empty(self.world, T, dr, dtype=x.dtype, device=x.device)
             self.backend.head_context(x, w_r, b_r, heads_r, causal, mask,
                                       out=chunks[self.rank].view(B, S, dr))
-            ops_ = [dist.P2POp(dist.irecv, chunks[r], r, group=self.group)
+            ops_ = [dist.P2POp(dist.irecv, chunks[r], self._peer(r), group=self.group)
                     for r in range(self.world) if r != self.dst]
             for req in (dist.batch_isend_irecv(ops_) if ops_ else []):
                 req.wait()
             return self.backend.out_proj_chunked(chunks, w_o, b_o, x, mask)
         ctx = self.backend.head_context(x, w_r, b_r, heads_r, causal, mask).reshape(T, dr).contiguous()
-        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, ctx, self.dst, group=self.group)]):
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, ctx, self._peer(self.dst), group=self.group)]):
             req.wait()
         return None
 
@@ -130,13 +139,13 @@ class ShardedAttention:
             out = torch.empty(global_batch, *local.shape[1:], dtype=local.dtype, device=local.device)
             starts = [shard_range(global_batch, self.world, r)[0] for r in range(self.world)]
             out[starts[self.rank]:starts[self.rank] + sizes[self.rank]].copy_(local)
-            ops_ = [dist.P2POp(dist.irecv, out[starts[r]:starts[r] + sizes[r]], r, group=self.group)
+            ops_ = [dist.P2POp(dist.irecv, out[starts[r]:starts[r] + sizes[r]], self._peer(r), group=self.group)
                     for r in range(self.world) if r != self.dst and sizes[r] > 0]
             for req in (dist.batch_isend_irecv(ops_) if ops_ else []):
                 req.wait()
             return out
         if sizes[self.rank] > 0:
-            for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, local.contiguous(), self.dst,
+            for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, local.contiguous(), self._peer(self.dst),
                                                           group=self.group)]):
                 req.wait()
         return None
