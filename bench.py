@@ -253,7 +253,16 @@ def cpu_reference_rate(cfg, seconds: float, seed: int = 1234):
 
 
 def run_reference(args, cfg):
-    rank, world, _ = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    """The reference arm: the reference algorithm (the oracle's fp32 restatement
+    of BaselineSelfAttention.forward + the block residual, checked against the
+    reference's own outputs by tests/test_oracle.py) on the host CPU with every
+    thread, on the SAME configuration as our arm.  Up to S = 8192 each step is
+    one forward of the whole configured batch (batch rows are evaluated a few at
+    a time when their score tables would not fit in host memory; rows never
+    interact, so the work and result are the whole batch's).  Longer sequences
+    cannot run densely; one step then is the streamed-oracle stripe of
+    cpu_reference_rate, extrapolated by FLOPs and labelled so."""
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
     if cfg.seq_len > 8192:
@@ -267,40 +276,35 @@ def run_reference(args, cfg):
                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
-    per_step = []
-    steps_total = args.warmup + args.steps
-    budget = max(0.2, 120.0 / steps_total)  # whole run within a few minutes
     from oracle import attention_layer_ref, generate_case, make_weights
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    x, _ = generate_case(1, cfg.seq_len, cfg.d_model, 1234)
-    w = make_weights(cfg.d_model, 1234)
+    B, S, D, H = cfg.batch, cfg.seq_len, cfg.d_model, cfg.num_heads
+    # score table + probabilities of one batch row: 2 * H * S^2 fp32; keep ~8 GB in flight
+    per_row = 2 * H * S * S * 4
+    chunk = max(1, min(B, (8 << 30) // per_row))
+    x, _ = generate_case(B, S, D, 1234, input_scale=cfg.input_scale)
+    w = make_weights(D, 1234)
+    per_step = []
     with torch.inference_mode():
-        for i in range(steps_total):
+        for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            n = 0
-            while True:
-                attention_layer_ref(x, w, cfg.num_heads, None, cfg.causal)
-                n += 1
-                if time.perf_counter() - t0 >= budget:
-                    break
+            attention_layer_ref(x, w, H, None, cfg.causal, batch_chunk=chunk)
             el = time.perf_counter() - t0
             if i >= args.warmup:
-                per_step.append((n * cfg.seq_len, el))
-    tok = sum(t for t, _ in per_step)
-    sec = sum(s for _, s in per_step)
-    value = tok / sec
+                per_step.append(el)
+    sec = sum(per_step)
+    value = B * S * len(per_step) / sec
+    sample = (f"every step one whole forward of the configured batch (B={B}, S={S}, D={D}, H={H}, fp32, "
+              f"{chunk} batch row(s) at a time), {len(per_step)} timed steps")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec / len(per_step),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, N(0,1) inputs, N(0,0.02) weights)",
-        "config": {"workload": cfg.name, "batch": cfg.batch, "seq_len": cfg.seq_len,
-                   "d_model": cfg.d_model, "heads": cfg.num_heads, "causal": cfg.causal,
-                   "sample": "each step: whole 1-row forwards for ~%.0fs" % budget},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"1 batch row (S={cfg.seq_len}) per forward, fp32, "
-                                   f"{len(per_step)} timed steps"},
+        "config": {"workload": cfg.name, "batch": B, "seq_len": S, "d_model": D, "heads": H,
+                   "causal": cfg.causal, "same_config_as_ours": True, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -402,6 +406,93 @@ def run_ours_heads(args, cfg, rank, world, local):
     return 0
 
 
+def run_ours_batch_strong(args, cfg, rank, world, local):
+    """Configurations 3 and 4 on N GPUs: the configured batch split over the ranks
+    (rank r runs rows shard_range(B, N, r) through the layer, strong scaling)
+    and every rank's output rows gathered into one [B,S,D] tensor on rank 0
+    with NCCL point-to-point receives, inside the timed region
+    (ShardedAttention "batch" mode)."""
+    from oracle import make_weights
+    from tiktok_techjam_2026_track3_b200 import B200AttentionLayer, ops
+    from tiktok_techjam_2026_track3_b200.config import attention_flops
+    from tiktok_techjam_2026_track3_b200.partition import ShardedAttention, shard_range
+    dev = torch.device("cuda", local)
+    dtype = cfg.torch_dtype
+    B, S, D, H = cfg.batch, cfg.seq_len, cfg.d_model, cfg.num_heads
+    r0, r1 = shard_range(B, world, rank)
+    layer = B200AttentionLayer(D, H, quant=cfg.quant)
+    layer.load_state_dict(make_weights(D, 1234).state_dict())
+    layer = layer.to(device=dev, dtype=dtype).eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    x = torch.randn(r1 - r0, S, D, generator=g, device=dev, dtype=dtype) * cfg.input_scale
+    sh = ShardedAttention(layer, "batch")
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step(ev):
+        ev[0].record(stream)
+        out = sh.backend.layer(layer, x, None, cfg.causal)
+        ev[1].record(stream)
+        sh._gather_rows(out, B)
+        ev[2].record(stream)
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    warm = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with torch.inference_mode():
+        for _ in range(max(1, args.warmup)):
+            step(warm)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        with ClockSampler(dev) as clk:
+            for i in range(args.steps):
+                flush.zero_()
+                barrier(world)
+                step(evs[i])
+            torch.cuda.synchronize(dev)
+        barrier(world)
+    ops.check_device_status(dev)
+    total_ms = max_over_ranks(sum(e[0].elapsed_time(e[2]) for e in evs), world)
+    ms_per_step = total_ms / args.steps
+    layer_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs), world)
+    gather_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    peaks = measured_peaks()
+    layer_tf = attention_flops(cfg) / (ms_per_step / 1e3) / 1e12
+    rows_max = max(shard_range(B, world, r)[1] - shard_range(B, world, r)[0] for r in range(world))
+    local_cfg = cfg.with_(batch=rows_max)
+    achieved = attention_flops(local_cfg) / (layer_ms / 1e3) / 1e12
+    # the slowest rank's layer against the time its kernels would take at their peaks
+    # (int8 projections against twice the bf16 dense peak)
+    proj = attention_flops(local_cfg) - attention_flops(local_cfg, include_projections=False)
+    peak_gemm = peaks["bf16_tflops"] * (2.0 if cfg.quant == "int8" else 1.0)
+    ideal_ms = 1e3 * (proj / (peak_gemm * 1e12)
+                      + attention_flops(local_cfg, include_projections=False) / (peaks["bf16_tflops"] * 1e12))
+    line = {
+        "metric": METRIC, "value": B * S / (ms_per_step / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": {"float16": "fp16", "bfloat16": "bf16"}[cfg.dtype] + ("+int8" if cfg.quant else ""),
+        "data": "synthetic (seeded; x ~ N(0,1), weights/biases ~ N(0,0.02))",
+        "config": {"workload": cfg.name, "batch": B, "rows_per_gpu": rows_max, "seq_len": S, "d_model": D,
+                   "heads": H, "causal": cfg.causal,
+                   "parallelism": f"batch split over {world} GPUs, NCCL gather of output rows to rank 0",
+                   "l2": "flushed between timed steps (256 MB write, outside the events)"},
+        "layer_tflops": layer_tf,
+        "layer_frac_of_peak": ideal_ms / layer_ms,
+        "kernels_ms": {"layer_slowest_rank": layer_ms, "gather_rank_local": gather_ms},
+        "roofline": {"kernel": "attention_layer (slowest rank)", "bound": "tensor", "achieved": achieved,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": ideal_ms / layer_ms,
+                     "peak_source": f"{peaks['source']} (bf16 dense burst; int8 GEMMs against 2x)",
+                     "traffic": None},
+        "gather_gbs": (B - (r1 - r0)) * S * D * 2 / (gather_ms / 1e3) / 1e9 if rank == 0 and world > 1 else None,
+        "gpu_launches": (5 if cfg.quant else 3) * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_ours(args, cfg):
     from oracle import make_weights  # only to seed weights identically to the tests
     from tiktok_techjam_2026_track3_b200 import B200AttentionLayer, ops
@@ -411,6 +502,10 @@ def run_ours(args, cfg):
     rank, world, local = init_dist(args.gpus)
     if cfg.shard == "heads" and world > 1:
         rc = run_ours_heads(args, cfg, rank, world, local)
+        torch.distributed.destroy_process_group()
+        return rc
+    if cfg.scaling == "strong" and world > 1:
+        rc = run_ours_batch_strong(args, cfg, rank, world, local)
         torch.distributed.destroy_process_group()
         return rc
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -539,9 +634,13 @@ def run_ours(args, cfg):
     ideal_ms = sum(fl / (pk * 1e12) * 1e3 for _, fl, pk in kernels.values())
     clocks = clk.summary()
 
-    # ---- e2e through the public module call, pinned host buffers
-    x_host = x.cpu().pin_memory()
-    out_host = torch.empty(x_host.shape, dtype=dtype).pin_memory()
+    # ---- e2e through the public module call, pinned host buffers allocated in
+    # memory local to this GPU's NUMA node
+    from tiktok_techjam_2026_track3_b200.pipeline import HostPipeline, near_device
+    with near_device(dev) as numa_node:
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty(x_host.shape, dtype=dtype).pin_memory()
+        outs_host = [torch.empty(x_host.shape, dtype=dtype).pin_memory() for _ in range(2)]
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     with torch.inference_mode():
@@ -566,8 +665,6 @@ def run_ours(args, cfg):
     # step i-1's output copy overlap step i's kernels.  Every step still copies
     # its input in from pinned host memory and its result back.  No L2 flush:
     # each step streams ~200 MB (input, qkv, ctx, output), more than the L2.
-    from tiktok_techjam_2026_track3_b200.pipeline import HostPipeline
-    outs_host = [torch.empty(x_host.shape, dtype=dtype).pin_memory() for _ in range(2)]
     pipe = HostPipeline(lambda xd: layer(xd, None, cfg.causal), dev, depth=2)
     with torch.inference_mode():
         pipe.run([x_host] * max(3, args.warmup), [outs_host[i % 2] for i in range(max(3, args.warmup))])
@@ -604,7 +701,7 @@ def run_ours(args, cfg):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nbytes,
                 "d2h_bytes_per_step": nbytes,
                 "mode": "B200AttentionLayer calls through HostPipeline (copies of steps i+1 / i-1 overlap step i)",
-                "serial_value": e2e_serial},
+                "serial_value": e2e_serial, "pinned_numa_node": numa_node},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }

@@ -66,7 +66,7 @@ CASES = [  # (B, S, H, hd, causal)
     # 8 and 32 (the reference's shapes.json with d_model 32 / 128), 256 (d_model 1024 over 4 heads)
     (3, 128, 4, 8, True), (2, 300, 16, 8, False), (4, 128, 4, 32, True), (2, 1000, 3, 32, False),
     (2, 33, 2, 16, True), (2, 500, 2, 96, True), (4, 128, 4, 256, True), (1, 700, 2, 256, False),
-    (2, 1100, 2, 256, True), (1, 300, 2, 200, True), (1, 32, 4, 32, True),
+    (2, 1100, 2, 256, True), (1, 300, 4, 200, True), (1, 32, 4, 32, True),
 ]
 
 

@@ -30,6 +30,7 @@ class LayerConfig:
     dtype: str = "float16"
     quant: Optional[str] = None      # None or "int8" (W8A8 projections)
     shard: str = "batch"             # how bench / partitioner split it over GPUs
+    scaling: str = "weak"            # multi-GPU bench: "weak" (batch per GPU) or "strong" (batch split)
     input_scale: float = 1.0
     weight_std: float = 0.02
 
@@ -60,6 +61,8 @@ class LayerConfig:
             raise ValueError("quant must be None or 'int8'")
         if self.shard not in ("batch", "heads"):
             raise ValueError("shard must be 'batch' or 'heads'")
+        if self.scaling not in ("weak", "strong"):
+            raise ValueError("scaling must be 'weak' or 'strong'")
 
     def with_(self, **kw) -> "LayerConfig":
         return replace(self, **kw)
@@ -83,11 +86,11 @@ PRESETS: Dict[int, LayerConfig] = {
     2: LayerConfig("cfg2_fp16_b8_s2048_d1024_h16_causal", 8, 2048, 1024, 16, causal=True,
                    dtype="float16"),
     3: LayerConfig("cfg3_int8_b16_s4096_d4096_h32_causal", 16, 4096, 4096, 32, causal=True,
-                   dtype="bfloat16", quant="int8"),
+                   dtype="bfloat16", quant="int8", scaling="strong"),
     4: LayerConfig("cfg4_bf16_b32_s100000_d512_h8_causal", 32, 100000, 512, 8, causal=True,
-                   dtype="bfloat16"),
+                   dtype="bfloat16", scaling="strong"),
     5: LayerConfig("cfg5_bf16_b1_s262144_d4096_h32_causal", 1, 262144, 4096, 32, causal=True,
-                   dtype="bfloat16", shard="heads"),
+                   dtype="bfloat16", shard="heads", scaling="strong"),
 }
 
 

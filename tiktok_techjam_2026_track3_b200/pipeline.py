@@ -16,11 +16,62 @@ the module on each batch in turn (tests/test_gpu_pipeline.py).
 
 from __future__ import annotations
 
-from typing import Callable, List, Sequence
+import contextlib
+import os
+from typing import Callable, Iterator, List, Optional, Sequence
 
 import torch
 
-__all__ = ["HostPipeline"]
+__all__ = ["HostPipeline", "device_numa_node", "near_device"]
+
+
+def _parse_cpulist(text: str) -> List[int]:
+    cpus: List[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.extend(range(int(a), int(b) + 1))
+        else:
+            cpus.append(int(part))
+    return cpus
+
+
+def device_numa_node(device: torch.device) -> Optional[int]:
+    """NUMA node of the GPU's PCI slot (Linux sysfs), or None if unknown."""
+    props = torch.cuda.get_device_properties(device)
+    try:
+        addr = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{addr}/numa_node") as f:
+            node = int(f.read().strip())
+    except (AttributeError, OSError, ValueError):
+        return None
+    return node if node >= 0 else None
+
+
+@contextlib.contextmanager
+def near_device(device: torch.device) -> Iterator[Optional[int]]:
+    """Run the body with this process's CPU affinity restricted to the CPUs of
+    the GPU's NUMA node, then restore it.  Pinned host buffers allocated inside
+    get their pages from memory local to that GPU (first touch by a thread on
+    that node), so their PCIe copies do not cross the socket interconnect.
+    Yields the node (None when it cannot be determined; nothing changes then)."""
+    node = device_numa_node(device)
+    old = None
+    if node is not None and hasattr(os, "sched_setaffinity"):
+        try:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                cpus = _parse_cpulist(f.read())
+            old = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, cpus)
+        except OSError:
+            old, node = None, None
+    try:
+        yield node
+    finally:
+        if old is not None:
+            os.sched_setaffinity(0, old)
 
 
 class HostPipeline:
