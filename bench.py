@@ -68,6 +68,10 @@ def parse_args():
     ap.add_argument("--block", action="store_true",
                     help="time one whole transformer block instead of the attention layer")
     ap.add_argument("--ffn-mult", type=int, default=4, help="ffn_dim = ffn_mult * d_model (--block)")
+    ap.add_argument("--shape", type=int, default=None, choices=range(1, 14),
+                    help="time an official whole-model shape (Project/shapes.json ids 1-13) instead")
+    ap.add_argument("--dtype", default="float32", choices=("float32", "float16", "bfloat16"),
+                    help="model dtype for --shape (the reference benchmark's default is float32)")
     return ap.parse_args()
 
 
@@ -827,8 +831,89 @@ def run_block(args, cfg):
     return 0
 
 
+def run_shape(args):
+    """One of the reference's 14 official whole-model shapes (Project/shapes.json)
+    through the drop-in model, timed as the reference benchmark times it (the
+    same input every call, an all-true valid_token_mask, CUDA events around
+    each forward; Ref :477-508): the default path (CUDA-graph replay from the
+    second call for launch-bound sizes), the same model eagerly, and the
+    PyTorch model of the oracle (BaselineTransformer restated, dense attention)
+    on the same GPU for context."""
+    import types
+    from oracle import generate_case
+    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef
+    from tiktok_techjam_2026_track3_b200 import ops, plugin
+    from tiktok_techjam_2026_track3_b200.config import OFFICIAL_SHAPES
+    sh = OFFICIAL_SHAPES[args.shape]
+    dev = torch.device("cuda", 0)
+    dtype = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}[args.dtype]
+    B = args.batch or sh.batch
+    cfg = TransformerConfigRef(batch_size=B, seq_len=sh.seq_len, d_model=sh.d_model, num_heads=sh.num_heads,
+                               ffn_dim=sh.ffn_dim, num_layers=sh.num_layers, causal=sh.causal)
+    torch.manual_seed(1234)
+    ref = BaselineTransformerRef(cfg)
+    otb = types.SimpleNamespace(BaselineTransformer=BaselineTransformerRef)
+    ours = plugin.build(otb, cfg)
+    ours.load_state_dict(ref.state_dict())
+    ours = ours.to(device=dev, dtype=dtype).eval()
+    ref = ref.to(device=dev, dtype=dtype).eval()
+    x, mask = generate_case(B, sh.seq_len, sh.d_model, 1234, dtype=dtype, device="cuda")
+    stream = torch.cuda.current_stream(dev)
+
+    def time_model(fn):
+        with torch.inference_mode():
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            torch.cuda.synchronize(dev)
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for a, b in evs:
+                a.record(stream)
+                fn()
+                b.record(stream)
+            torch.cuda.synchronize(dev)
+        return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+    with ClockSampler(dev) as clk:
+        graph_ms = time_model(lambda: ours(x, mask))
+    ours.ttj_cuda_graphs = False
+    eager_ms = time_model(lambda: ours(x, mask))
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True  # the reference script's CUDA setting (Ref :687-688)
+    try:
+        torch_ms = time_model(lambda: ref(x, mask))
+    except torch.cuda.OutOfMemoryError:
+        torch_ms = None
+    torch.backends.cuda.matmul.allow_tf32 = old_tf32
+    ops.check_device_status(dev)
+    T = B * sh.seq_len
+    D, F, L = sh.d_model, sh.ffn_dim, sh.num_layers
+    flops = L * (2.0 * T * D * 4 * D + 2.0 * 2 * T * D * F
+                 + 4.0 * B * sh.num_heads * sh.seq_len ** 2 * (D // sh.num_heads) * (0.5 if sh.causal else 1.0))
+    launches = L * 7 + 1 + (2 if dtype == torch.float32 else 0)
+    line = {
+        "metric": f"whole-model forward tokens/s, official shape {args.shape}", "value": T / (graph_ms / 1e3),
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": graph_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
+        "data": "synthetic (seeded; x ~ N(0,1); nn.Linear / nn.LayerNorm default init, seeded)",
+        "config": {"workload": f"shape{args.shape}_b{B}_s{sh.seq_len}_d{D}_h{sh.num_heads}_l{L}_f{F}_causal",
+                   "same_input_every_call": True, "valid_token_mask": "all true"},
+        "model_tflops": flops / (graph_ms / 1e3) / 1e12,
+        "eager": {"ms_per_step": eager_ms, "value": T / (eager_ms / 1e3)},
+        "torch_reference_model_same_gpu": (None if torch_ms is None else
+                                           {"ms_per_step": torch_ms, "value": T / (torch_ms / 1e3),
+                                            "note": "dense PyTorch BaselineTransformer, TF32 allowed as Ref :687-688"}),
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
+    if args.shape is not None:
+        return run_shape(args)
     from tiktok_techjam_2026_track3_b200.config import PRESETS
     cfg = PRESETS[args.config]
     if args.batch:

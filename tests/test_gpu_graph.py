@@ -53,3 +53,53 @@ def test_captured_forward_replays_exactly(quant, dtype, D, H, masked):
             eager = layer(x.cuda(), mask, True)
             torch.cuda.synchronize()
             assert torch.equal(static_out, eager)
+
+
+@pytest.mark.parametrize("sid,dtype", [(2, torch.float32), (7, torch.float16), (8, torch.bfloat16),
+                                       (12, torch.float32)])
+def test_plugin_model_graph_replay_equals_eager(sid, dtype):
+    """The drop-in model replays a captured CUDA graph from the second call with
+    the same shape / mask presence / weights on (the reference route's behaviour,
+    dispatcher_region.py:1220-1260).  Every call must equal an eager call of the
+    same model bit for bit, return a fresh tensor, follow new inputs and masks,
+    and pick up new weights."""
+    import types
+    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef
+    from tiktok_techjam_2026_track3_b200 import plugin
+    from tiktok_techjam_2026_track3_b200.config import OFFICIAL_SHAPES
+    sh = OFFICIAL_SHAPES[sid]
+    B = min(sh.batch, 3)
+    cfg = TransformerConfigRef(batch_size=B, seq_len=sh.seq_len, d_model=sh.d_model, num_heads=sh.num_heads,
+                               ffn_dim=sh.ffn_dim, num_layers=sh.num_layers, causal=True)
+    otb = types.SimpleNamespace(BaselineTransformer=BaselineTransformerRef)
+    torch.manual_seed(sid)
+    sd = BaselineTransformerRef(cfg).state_dict()
+    model = plugin.build(otb, cfg)
+    model.load_state_dict(sd)
+    model = model.to(device="cuda", dtype=dtype).eval()
+    eager = plugin.build(otb, cfg)
+    eager.load_state_dict(sd)
+    eager = eager.to(device="cuda", dtype=dtype).eval()
+    eager.ttj_cuda_graphs = False
+    cases = []
+    for i, pad in enumerate((0.0, 0.0, 0.0, 0.3, 0.3, 0.3, 0.0)):
+        x, m = generate_case(B, cfg.seq_len, cfg.d_model, 4000 + i, dtype=dtype, padding_ratio=pad)
+        cases.append((x.cuda(), m.cuda() if pad > 0 else None))
+    outs = []
+    with torch.inference_mode():
+        for x, m in cases:
+            out = model(x, m)
+            ref = eager(x, m)
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref)
+            assert all(out.data_ptr() != o.data_ptr() for o in outs)
+            outs.append(out)
+    assert model.__dict__["_ttj_graph_runner"].graph is not None  # replays happened
+    # new weights: the next calls follow them (eager, then a new capture)
+    sd2 = {k: v * 1.5 for k, v in sd.items()}
+    model.load_state_dict(sd2)
+    eager.load_state_dict(sd2)
+    with torch.inference_mode():
+        for x, m in cases[:3]:
+            out = model(x, m)
+            assert torch.equal(out, eager(x, m))

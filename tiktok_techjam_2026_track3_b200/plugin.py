@@ -12,29 +12,36 @@ harness loads candidates through a module-level ``build(otb, config)`` where
 ``BaselineTransformer`` (so the module tree and state-dict keys are the
 reference's) and runs its forward on the sm_100a kernels.
 
-fp16 / bf16 models run each ``BaselineTransformerBlock`` (Ref:134-145) as one
+Every ``BaselineTransformerBlock`` (Ref:134-145) is one
 ``ttj_transformer_block_fwd`` call: LayerNorm, QKV GEMM, flash attention,
 out-proj GEMM with bias + mask + residual, LayerNorm, ffn_in GEMM with bias +
 exact GELU, ffn_out GEMM with bias + residual + the block's row zeroing; the
 final norm and its masked_fill (Ref:169-171) are one LayerNorm launch.
+fp16 / bf16 models run in their own dtype.  fp32 models (the benchmark's
+default dtype) run the same kernels on fp16 copies of the parameters and of
+the input (fp32 accumulation inside every kernel) and return fp32, as the
+reference's own optimised route does for fp32 models
+(Project/submission/dispatcher_region.py:760-801 packs fp16 weights); the GPU
+tests hold the result to the benchmark's tolerance against the fp32 reference.
 
-fp32 models (the benchmark's default dtype) run the attention sublayer with
-fp16 tensor-core operands and fp32 accumulation, added to the fp32 residual in
-fp32; LayerNorm and the FFN stay the reference's own fp32 torch modules.
-Whether that meets the benchmark's tolerance is checked by the GPU tests
-against the fp32 reference.
+Repeated calls with the same input shape, dtype, mask presence and weights are
+replayed from a CUDA graph captured on the second such call (the reference's
+route does the same, dispatcher_region.py:1220-1260): the input (and mask) are
+copied into the graph's static buffers and the output is returned as a fresh
+copy, never the graph's own buffer.  Only launch-bound sizes (at most 2^24
+activation elements) are captured; larger calls run eagerly, where launch
+overhead is negligible.  ``model.ttj_cuda_graphs = False`` turns capture off.
 """
 
 from __future__ import annotations
 
-from typing import Dict, Optional
+from typing import Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import ops
-from .layer import B200SelfAttention
+from .layer import B200SelfAttention, _version
 
 __all__ = ["make_user_optimized_transformer", "build", "attention_sublayer"]
 
@@ -62,87 +69,127 @@ def attention_sublayer(block: nn.Module) -> B200SelfAttention:
     return attn
 
 
-def _attention_residual(block, x: torch.Tensor, mask: Optional[torch.Tensor], causal: bool) -> torch.Tensor:
-    attn = attention_sublayer(block)
-    h = block.norm1(x)
-    if x.dtype in (torch.float16, torch.bfloat16):
-        return attn.forward_residual(h, x, mask, causal)
-    if x.dtype != torch.float32:
-        raise RuntimeError(f"unsupported dtype {x.dtype}")
-    # fp32 model: fp16 operands on the tensor cores, fp32 accumulate, fp32 residual.
-    half = _half_view(attn)
-    return x + half.forward(h.to(torch.float16), mask, causal).float()
+_GRAPH_MAX_ELEMENTS = 1 << 24
 
 
-def _half_view(attn: B200SelfAttention) -> B200SelfAttention:
-    """An fp16 copy of the projection weights for fp32 models (rebuilt when the
-    fp32 weights change)."""
-    from .layer import _version
-    key = tuple((p.data_ptr(), _version(p)) for p in attn._params())
-    cached = attn.__dict__.get("_ttj_half")
-    if cached is not None and cached[0] == key:
-        return cached[1]
-    with torch.inference_mode(False), torch.no_grad():
-        half = B200SelfAttention(attn.d_model, attn.num_heads).to(device=attn.q_proj.weight.device)
-        for dst, src in zip(half._params(), attn._params()):
-            dst.copy_(src.detach().clone() if src.is_inference() else src)
-        half = half.half()
-    attn.__dict__["_ttj_half"] = (key, half)
-    return half
+def _compute_dtype(dtype: torch.dtype) -> torch.dtype:
+    if dtype in (torch.float16, torch.bfloat16):
+        return dtype
+    if dtype == torch.float32:
+        return torch.float16
+    raise RuntimeError(f"unsupported dtype {dtype}: the sm_100a kernels take float32, float16 or bfloat16 models")
 
 
-def _block_params(block) -> Dict[str, torch.Tensor]:
-    """The block's parameters in the kernels' layout (q|k|v packed), cached and
-    rebuilt when any parameter's storage or version changes."""
-    from .layer import _version
+def _block_params(block, dtype: torch.dtype) -> Dict[str, torch.Tensor]:
+    """The block's parameters in the kernels' layout (q|k|v packed) and compute
+    dtype, cached and rebuilt when any parameter's storage or version changes."""
     att = block.attention
     src = (block.norm1.weight, block.norm1.bias, att.q_proj.weight, att.q_proj.bias,
            att.k_proj.weight, att.k_proj.bias, att.v_proj.weight, att.v_proj.bias,
            att.out_proj.weight, att.out_proj.bias, block.norm2.weight, block.norm2.bias,
            block.ffn_in.weight, block.ffn_in.bias, block.ffn_out.weight, block.ffn_out.bias)
-    key = tuple((t.data_ptr(), _version(t), t.dtype) for t in src)
+    key = (dtype,) + tuple((t.data_ptr(), _version(t), t.dtype) for t in src)
     cached = block.__dict__.get(_BLOCK_ATTR)
     if cached is not None and cached[0] == key:
         return cached[1]
     with torch.no_grad():
-        t = [p.detach() for p in src]
+        t = [p.detach().to(dtype) for p in src]
         packed = {
-            "ln1_w": t[0], "ln1_b": t[1],
+            "ln1_w": t[0].contiguous(), "ln1_b": t[1].contiguous(),
             "w_qkv": torch.cat([t[2], t[4], t[6]], 0).contiguous(),
             "b_qkv": torch.cat([t[3], t[5], t[7]], 0).contiguous(),
-            "w_o": t[8].contiguous(), "b_o": t[9], "ln2_w": t[10], "ln2_b": t[11],
-            "w_in": t[12].contiguous(), "b_in": t[13], "w_out": t[14].contiguous(), "b_out": t[15],
+            "w_o": t[8].contiguous(), "b_o": t[9].contiguous(), "ln2_w": t[10].contiguous(),
+            "ln2_b": t[11].contiguous(), "w_in": t[12].contiguous(), "b_in": t[13].contiguous(),
+            "w_out": t[14].contiguous(), "b_out": t[15].contiguous(),
         }
     block.__dict__[_BLOCK_ATTR] = (key, packed)
     return packed
 
 
-def _block_forward(block, x, mask, causal):
-    if x.dtype in (torch.float16, torch.bfloat16):
-        return ops.transformer_block(x, _block_params(block), block.attention.num_heads, causal,
-                                     block.norm1.eps, block.norm2.eps, mask)
-    x = _attention_residual(block, x, mask, causal)
-    x = x + block.ffn_out(F.gelu(block.ffn_in(block.norm2(x)), approximate="none"))
-    if mask is not None:
-        x = x.masked_fill(~mask[..., None], 0)
-    return x
+def _final_norm_params(model, dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    fn = model.final_norm
+    key = (dtype, fn.weight.data_ptr(), _version(fn.weight), fn.bias.data_ptr(), _version(fn.bias))
+    cached = model.__dict__.get("_ttj_final_norm")
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    with torch.no_grad():
+        wb = (fn.weight.detach().to(dtype).contiguous(), fn.bias.detach().to(dtype).contiguous())
+    model.__dict__["_ttj_final_norm"] = (key, wb)
+    return wb
+
+
+def _model_forward(model, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+    """Blocks + final norm on the kernels, in the compute dtype of x's dtype."""
+    cdt = _compute_dtype(x.dtype)
+    h = x if x.dtype == cdt else x.to(cdt)
+    for layer in model.layers:
+        h = ops.transformer_block(h, _block_params(layer, cdt), layer.attention.num_heads,
+                                  model.config.causal, layer.norm1.eps, layer.norm2.eps, mask)
+    w, b = _final_norm_params(model, cdt)
+    out = ops.layernorm(h, w, b, model.final_norm.eps, row_mask=mask)
+    return out if out.dtype == x.dtype else out.to(x.dtype)
+
+
+def _weights_key(model):
+    return tuple((p.data_ptr(), _version(p), p.dtype) for p in model.parameters())
+
+
+class _GraphRunner:
+    """One captured forward per model: (shape, dtype, device, mask presence,
+    weights) must match for a replay; a new key runs eagerly once and is
+    captured on its second call."""
+
+    def __init__(self) -> None:
+        self.key = None
+        self.pending = None
+        self.graph = None
+        self.static_x = None
+        self.static_mask = None
+        self.static_out = None
+
+    def __call__(self, model, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        key = (tuple(x.shape), x.dtype, x.device, None if mask is None else tuple(mask.shape),
+               _weights_key(model))
+        if self.graph is not None and key == self.key:
+            self.static_x.copy_(x)
+            if mask is not None:
+                self.static_mask.copy_(mask)
+            self.graph.replay()
+            return self.static_out.clone()
+        if key != self.pending:
+            self.pending = key
+            return _model_forward(model, x, mask)   # first call: eager (packs weights)
+        # second call with this key: capture
+        self.graph = None
+        self.static_x = x.clone()
+        self.static_mask = None if mask is None else mask.clone()
+        graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(x.device)
+        with torch.cuda.graph(graph):
+            self.static_out = _model_forward(model, self.static_x, self.static_mask)
+        self.graph, self.key, self.pending = graph, key, None
+        self.graph.replay()
+        return self.static_out.clone()
 
 
 def make_user_optimized_transformer(base_cls):
-    """Subclass of the reference's BaselineTransformer with the sm_100a attention."""
+    """Subclass of the reference's BaselineTransformer on the sm_100a kernels."""
 
     class UserOptimizedTransformer(base_cls):
+        ttj_cuda_graphs = True
+
         def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+            if not x.is_cuda:
+                raise RuntimeError(f"x must be a CUDA tensor (got {x.device}); there is no CPU path")
             mask = None if valid_token_mask is None else valid_token_mask.to(torch.bool)
-            for layer in self.layers:
-                x = _block_forward(layer, x, mask, self.config.causal)
-            if x.dtype in (torch.float16, torch.bfloat16):
-                fn = self.final_norm
-                return ops.layernorm(x, fn.weight.detach(), fn.bias.detach(), fn.eps, row_mask=mask)
-            x = self.final_norm(x)
-            if mask is not None:
-                x = x.masked_fill(~mask[..., None], 0)
-            return x
+            if (self.ttj_cuda_graphs and x.is_contiguous() and x.numel() <= _GRAPH_MAX_ELEMENTS
+                    and not torch.cuda.is_current_stream_capturing()):
+                runner = self.__dict__.get("_ttj_graph_runner")
+                if runner is None:
+                    runner = _GraphRunner()
+                    self.__dict__["_ttj_graph_runner"] = runner
+                return runner(self, x.contiguous(), mask)
+            return _model_forward(self, x, mask)
 
     UserOptimizedTransformer.__name__ = "UserOptimizedTransformer"
     UserOptimizedTransformer.__qualname__ = "UserOptimizedTransformer"
