@@ -641,7 +641,7 @@ def run_ours(args, cfg):
     # ---- e2e through the public module call, pinned host buffers allocated in
     # memory local to this GPU's NUMA node
     from tiktok_techjam_2026_track3_b200.pipeline import HostPipeline, near_device
-    with near_device(dev) as numa_node:
+    with near_device(dev) as local_cpus:
         x_host = x.cpu().pin_memory()
         out_host = torch.empty(x_host.shape, dtype=dtype).pin_memory()
         outs_host = [torch.empty(x_host.shape, dtype=dtype).pin_memory() for _ in range(2)]
@@ -705,7 +705,8 @@ def run_ours(args, cfg):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nbytes,
                 "d2h_bytes_per_step": nbytes,
                 "mode": "B200AttentionLayer calls through HostPipeline (copies of steps i+1 / i-1 overlap step i)",
-                "serial_value": e2e_serial, "pinned_numa_node": numa_node},
+                "serial_value": e2e_serial,
+                "pinned_near_cpus": None if local_cpus is None else f"{len(local_cpus)} CPUs ({local_cpus[0]}-{local_cpus[-1]})"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }

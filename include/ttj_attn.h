@@ -42,7 +42,11 @@ extern "C" {
 
 typedef struct CUstream_st* ttj_stream_t; /* == cudaStream_t; NULL = legacy default stream */
 
-enum ttj_dtype { TTJ_F16 = 0, TTJ_BF16 = 1 };
+enum ttj_dtype {
+  TTJ_F16 = 0,
+  TTJ_BF16 = 1,
+  TTJ_F32 = 2  /* fp32 residual stream: only where an entry point says so */
+};
 
 enum ttj_status {
   TTJ_OK = 0,
@@ -261,7 +265,8 @@ int ttj_int8_attn_layer_fwd(const ttj_int8_attn_layer_args* args, ttj_stream_t s
  * torch_transformer_benchmark.py:128-130 (norm1, norm2) and :159 (final_norm).
  * Rows with row_mask[r] == 0 are written as zeros (the model's final
  * masked_fill, :170-171); row_mask may be NULL.  gamma/beta are [d] in the same
- * dtype as x.  Requires d % 8 == 0 and d <= 8192.
+ * dtype as x.  Requires d % 8 == 0 and d <= 8192.  dtype TTJ_F32: x, gamma,
+ * beta and y are all fp32 (d <= 4096), e.g. the final norm of an fp32 model.
  */
 int ttj_layernorm_fwd(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask,
                       void* y, int64_t rows, int64_t d, float eps, int dtype, ttj_stream_t stream);
@@ -317,6 +322,17 @@ size_t ttj_block_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model,
  * bias+mask+residual, LayerNorm, ffn_in GEMM with bias+GELU, ffn_out GEMM with
  * bias+residual and the block's final row zeroing (masked_fill, :143-144).
  * Requires ffn_dim % 32 == 0 plus the attention layer's shape rules.
+ *
+ * dtype TTJ_F32 runs the block of an fp32 model with an fp32 residual stream
+ * and fp16 tensor-core operands: x, out, ln1_w/ln1_b, ln2_w/ln2_b, b_o and
+ * b_out are fp32; w_qkv, b_qkv, w_o, w_in, b_in and w_out are fp16.  The
+ * LayerNorms read the fp32 stream and write fp16 GEMM operands; the out-proj
+ * and ffn_out epilogues add their fp32 bias and residual in fp32 and write the
+ * fp32 stream.  d_model <= 4096.  The reference's optimised route runs fp32
+ * models on fp16 kernels with an fp16 stream
+ * (Project/submission/dispatcher_region.py:760-801); kept in fp32, the stream
+ * meets the benchmark tolerance on the official shapes where an fp16 stream
+ * misses it on a few elements.
  */
 int ttj_transformer_block_fwd(const ttj_block_args* args, ttj_stream_t stream);
 

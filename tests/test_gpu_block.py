@@ -123,7 +123,7 @@ def test_block_against_fp32_and_reference_run(dt, D, H, Fdim, masked):
     mcuda = None if mask is None else mask.cuda()
     with torch.inference_mode():
         base = ref16(x.cuda(), mcuda, True, in_dtype=True).float().cpu()
-        out = plugin._block_forward(blk16, x.cuda(), mcuda, True).float().cpu()
+        out = plugin.block_forward(blk16, x.cuda(), mcuda, True).float().cpu()
     if mask is not None:
         assert bool((out[~mask] == 0).all())
     err_ours = (out - target).abs()
@@ -132,3 +132,42 @@ def test_block_against_fp32_and_reference_run(dt, D, H, Fdim, masked):
           f"reference {dt} run max {err_base.max():.3g} mean {err_base.mean():.3g}")
     assert float(err_ours.mean()) <= 1.5 * float(err_base.mean()) + 1e-4
     assert float(err_ours.max()) <= 2.0 * float(err_base.max()) + 1e-3
+
+
+@pytest.mark.parametrize("rows,d", [(1, 32), (37, 128), (1031, 1024), (64, 4096)])
+def test_layernorm_fp32_stream(rows, d):
+    """LayerNorm over fp32 rows (the residual stream of an fp32 model) with fp32
+    gamma/beta, written in fp32: against torch's fp32 LayerNorm."""
+    g = torch.Generator().manual_seed(rows + d)
+    x = torch.randn(rows, d, generator=g) * 3 + 2
+    w = 1 + 0.1 * torch.randn(d, generator=g)
+    b = 0.1 * torch.randn(d, generator=g)
+    mask = torch.rand(rows, generator=g) > 0.2
+    mask[0] = True
+    out = ops.layernorm(x.cuda(), w.cuda(), b.cuda(), 1e-5, row_mask=mask.cuda()).cpu()
+    ref = F.layer_norm(x, (d,), w, b, 1e-5)
+    assert out.dtype == torch.float32
+    torch.testing.assert_close(out[mask], ref[mask], rtol=2e-5, atol=2e-5)
+    assert bool((out[~mask] == 0).all())
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_block_fp32_stream_against_fp32_module(masked):
+    """One block of an fp32 model (fp32 residual stream, fp16 tensor-core
+    operands) against the fp32 reference block on the unrounded parameters."""
+    B, S, D, H, Fdim = 2, 384, 256, 4, 1024
+    torch.manual_seed(3)
+    blk = BaselineTransformerBlockRef(D, H, Fdim).eval()
+    x = torch.randn(B, S, D, generator=torch.Generator().manual_seed(D))
+    mask = None
+    if masked:
+        mask = torch.ones(B, S, dtype=torch.bool)
+        mask[1, 250:] = False
+    with torch.inference_mode():
+        ref = blk(x, mask, True)
+    dev = blk.to("cuda")
+    with torch.inference_mode():
+        out = plugin.block_forward(dev, x.cuda(), None if mask is None else mask.cuda(), True)
+    assert out.dtype == torch.float32
+    rep = compare_outputs(ref, out.cpu())
+    assert rep.passed, str(rep)

@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libttj_attn_sm100.so"
 
 TTJ_F16 = 0
 TTJ_BF16 = 1
+TTJ_F32 = 2
 
 STATUS_NAMES = {
     0: "TTJ_OK", -1: "TTJ_ERR_INVALID_ARG", -2: "TTJ_ERR_UNSUPPORTED",

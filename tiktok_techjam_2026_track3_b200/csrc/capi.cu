@@ -392,14 +392,17 @@ int ttj_int8_attn_layer_fwd(const ttj_int8_attn_layer_args* a, ttj_stream_t stre
 
 int ttj_layernorm_fwd(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask,
                       void* y, int64_t rows, int64_t d, float eps, int dtype, ttj_stream_t stream) {
-  if (int rc = check_dtype(dtype)) return rc;
+  if (dtype != TTJ_F32)
+    if (int rc = check_dtype(dtype)) return rc;
   TTJ_CHECK_ARG(x && gamma && beta && y, TTJ_ERR_INVALID_ARG, "x, gamma, beta and y must be non-NULL");
   TTJ_CHECK_ARG(rows > 0 && d > 0, TTJ_ERR_INVALID_ARG, "rows and d must be positive");
   TTJ_CHECK_ARG(eps >= 0.f, TTJ_ERR_INVALID_ARG, "eps must be non-negative");
-  TTJ_CHECK_ARG(d % 8 == 0 && d <= 8192, TTJ_ERR_UNSUPPORTED, "d must be a multiple of 8 and at most 8192");
+  TTJ_CHECK_ARG(d % 8 == 0 && d <= (dtype == TTJ_F32 ? 4096 : 8192), TTJ_ERR_UNSUPPORTED,
+                "d must be a multiple of 8 and at most 8192 (4096 for fp32)");
   TTJ_CHECK_ARG(aligned16(x) && aligned16(gamma) && aligned16(beta) && aligned16(y), TTJ_ERR_ALIGNMENT,
                 "x, gamma, beta and y must be 16-byte aligned");
-  return ttj::launch_layernorm(x, gamma, beta, row_mask, y, rows, d, eps, dtype, (cudaStream_t)stream);
+  return ttj::launch_layernorm(x, gamma, beta, row_mask, y, rows, d, eps, dtype, (cudaStream_t)stream,
+                               dtype);
 }
 
 int ttj_linear_gelu_fwd(const void* x, const void* w, const void* bias, void* y, int64_t m, int64_t n,
@@ -433,15 +436,19 @@ size_t ttj_block_workspace_size(int64_t batch, int64_t seq_len, int64_t d_model,
   if (!size_args_ok(batch, seq_len, d_model) || ffn_dim <= 0 || ffn_dim >= (1ll << 31)) return 0;
   const size_t t = (size_t)batch * (size_t)seq_len, d = (size_t)d_model, f = (size_t)ffn_dim;
   const size_t wide = 3 * d > f ? 3 * d : f;
+  const size_t stream_bytes = dtype == TTJ_F32 ? 4 : 2;
   return round_up(t * d * 2, 256)        /* normalised input (norm1, then norm2) */
          + round_up(t * wide * 2, 256)   /* qkv, then the GELU activations */
          + round_up(t * d * 2, 256)      /* attention context */
-         + round_up(t * d * 2, 256);     /* x1 = x + attention */
+         + round_up(t * d * stream_bytes, 256);  /* x1 = x + attention (residual stream) */
 }
 
 int ttj_transformer_block_fwd(const ttj_block_args* a, ttj_stream_t stream) {
   TTJ_CHECK_ARG(a != nullptr, TTJ_ERR_INVALID_ARG, "args is NULL");
-  if (int rc = check_dtype(a->dtype)) return rc;
+  const bool f32 = a->dtype == TTJ_F32;  // fp32 residual stream, fp16 operands inside
+  if (!f32)
+    if (int rc = check_dtype(a->dtype)) return rc;
+  TTJ_CHECK_ARG(!f32 || a->d_model <= 4096, TTJ_ERR_UNSUPPORTED, "fp32 residual stream: d_model at most 4096");
   if (int rc = check_layer_shape(a->batch, a->seq_len, a->d_model, a->num_heads)) return rc;
   TTJ_CHECK_ARG(a->ffn_dim > 0 && a->ffn_dim % 32 == 0 && a->ffn_dim < (1ll << 31), TTJ_ERR_UNSUPPORTED,
                 "ffn_dim must be a positive multiple of 32");
@@ -462,6 +469,7 @@ int ttj_transformer_block_fwd(const ttj_block_args* a, ttj_stream_t stream) {
   TTJ_CHECK_ARG(aligned16(a->workspace), TTJ_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
   const int64_t T = a->batch * a->seq_len, D = a->d_model, F = a->ffn_dim;
   const size_t wide = (size_t)(3 * D > F ? 3 * D : F);
+  const int op = f32 ? TTJ_F16 : a->dtype;        // tensor-core operand / activation type
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   void* h = ws;                                   // norm1(x), later norm2(x1)
   ws += round_up((size_t)T * D * 2, 256);
@@ -469,37 +477,48 @@ int ttj_transformer_block_fwd(const ttj_block_args* a, ttj_stream_t stream) {
   ws += round_up((size_t)T * wide * 2, 256);
   void* ctx = ws;
   ws += round_up((size_t)T * D * 2, 256);
-  void* x1 = ws;
+  void* x1 = ws;                                  // residual stream after attention
   const uint8_t* mask = a->valid_token_mask;
-  int rc = ttj_layernorm_fwd(a->x, a->ln1_w, a->ln1_b, nullptr, h, T, D, a->eps1, a->dtype, stream);
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = f32 ? ttj::launch_layernorm(a->x, a->ln1_w, a->ln1_b, nullptr, h, T, D, a->eps1, TTJ_F32, st, op)
+               : ttj_layernorm_fwd(a->x, a->ln1_w, a->ln1_b, nullptr, h, T, D, a->eps1, a->dtype, stream);
   if (rc) return rc;
-  rc = ttj_qkv_proj_fwd(h, a->w_qkv, a->b_qkv, big, T, D, a->dtype, a->status, stream);
+  rc = ttj_qkv_proj_fwd(h, a->w_qkv, a->b_qkv, big, T, D, op, a->status, stream);
   if (rc) return rc;
   rc = ttj_flash_attn_fwd(big, mask, ctx, a->batch, a->seq_len, a->num_heads, D / a->num_heads, a->causal,
-                          a->dtype, a->status, stream);
+                          op, a->status, stream);
   if (rc) return rc;
-  rc = ttj_linear_fwd(ctx, a->w_o, a->b_o, a->x, mask, x1, T, D, D, a->dtype, a->status, stream);
+  // x1 = x + mask(ctx w_o^T + b_o), in the residual stream's type
+  ttj::GemmArgs g{};
+  g.a = ctx;
+  g.b = a->w_o;
+  g.bias = a->b_o;
+  g.residual = a->x;
+  g.row_mask = mask;
+  g.out = x1;
+  g.m = T;
+  g.n = D;
+  g.k = D;
+  g.in_dtype = op;
+  g.out_dtype = a->dtype;
+  g.epi = ttj::Epi::kBiasResidual;
+  g.status = a->status;
+  rc = ttj::launch_gemm(g, st);
   if (rc) return rc;
-  rc = ttj_layernorm_fwd(x1, a->ln2_w, a->ln2_b, nullptr, h, T, D, a->eps2, a->dtype, stream);
+  rc = f32 ? ttj::launch_layernorm(x1, a->ln2_w, a->ln2_b, nullptr, h, T, D, a->eps2, TTJ_F32, st, op)
+           : ttj_layernorm_fwd(x1, a->ln2_w, a->ln2_b, nullptr, h, T, D, a->eps2, a->dtype, stream);
   if (rc) return rc;
-  rc = ttj_linear_gelu_fwd(h, a->w_in, a->b_in, big, T, F, D, a->dtype, a->status, stream);
+  rc = ttj_linear_gelu_fwd(h, a->w_in, a->b_in, big, T, F, D, op, a->status, stream);
   if (rc) return rc;
   // out = mask_rows(x1 + ffn_out(.)): rows of invalid tokens become zero
-  ttj::GemmArgs g{};
   g.a = big;
   g.b = a->w_out;
   g.bias = a->b_out;
   g.residual = x1;
-  g.row_mask = mask;
   g.out = a->out;
-  g.m = T;
-  g.n = D;
   g.k = F;
-  g.in_dtype = a->dtype;
-  g.out_dtype = a->dtype;
   g.epi = ttj::Epi::kBiasResidualZeroRows;
-  g.status = a->status;
-  return ttj::launch_gemm(g, (cudaStream_t)stream);
+  return ttj::launch_gemm(g, st);
 }
 
 }  // extern "C"

@@ -172,6 +172,76 @@ __device__ __forceinline__ void gelu_erf_pair(float& v0, float& v1) {
   x2_split(x2_mul(x2_mul(v, x2(0.5f, 0.5f)), one_p_erf), v0, v1);
 }
 
+// fp32-output epilogue (16-bit operands, fp32 bias, fp32 residual and output):
+// the residual stream of an fp32 model.  Same data path as the 16-bit one, with
+// 32-column boxes (128 bytes of fp32 per row) instead of 64.
+//   kBias                  y = mask(acc + bias)
+//   kBiasResidual          y = residual + mask(acc + bias)
+//   kBiasResidualZeroRows  y = mask(residual + acc + bias)
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile_f32(const GemmParams& p, const CUtensorMap* tm_out,
+                                                  const CUtensorMap* tm_res, uint32_t t_row, int row0,
+                                                  int n_blk, int col_half, EpiState& es,
+                                                  int* status, volatile int* abort_flag) {
+  constexpr bool kZeroRows = EPI == (int)Epi::kBiasResidualZeroRows;
+  constexpr bool kResidual = EPI == (int)Epi::kBiasResidual || kZeroRows;
+  static_assert(kResidual || EPI == (int)Epi::kBias, "fp32 output: bias / residual epilogues only");
+  constexpr int kChunks = BN / 32 / 2;
+  const int lane = threadIdx.x & 31;
+  const int m = row0 + lane;
+  if (row0 >= p.M) return;  // the warp's 32 rows are all past the last row (uniform)
+  bool row_keep = true;
+  if (m < p.M && p.row_mask != nullptr) row_keep = __ldg(p.row_mask + m) != 0;
+#pragma unroll 1
+  for (int cc = 0; cc < kChunks; ++cc) {
+    const int c = col_half * kChunks + cc;
+    const int n0 = n_blk * BN + c * 32;
+    const int b = es.next;
+    if (kEpiBufs == 2) es.next ^= 1;
+    uint8_t* buf = b ? es.buf1 : es.buf0;
+    uint64_t* bar = b ? es.bar1 : es.bar0;
+    if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();
+    __syncwarp();
+    if (n0 >= p.N) continue;  // whole chunk past the last column (uniform)
+    if constexpr (kResidual) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar, kEpiBoxBytes);
+        tma_load_2d(buf, tm_res, bar, n0, row0);
+      }
+    }
+    uint32_t r[32];
+    tmem_ld32(t_row + c * 32, r);  // warp-collective
+    if constexpr (kResidual) {
+      const uint32_t ph = b ? es.phase1 : es.phase0;
+      if (!mbar_wait_warp<true>(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
+      if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // 16-byte slot q: columns n0 + 4q .. +3 (N % 32 == 0: all valid)
+      const float4 bias = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + n0 + 4 * q));
+      float v[4] = {__uint_as_float(r[4 * q]) + bias.x, __uint_as_float(r[4 * q + 1]) + bias.y,
+                    __uint_as_float(r[4 * q + 2]) + bias.z, __uint_as_float(r[4 * q + 3]) + bias.w};
+      float4* slot = reinterpret_cast<float4*>(buf + swz(lane, q));
+      if constexpr (kResidual) {
+        const float4 res = *slot;
+        const float rr[4] = {res.x, res.y, res.z, res.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = row_keep ? rr[i] + v[i] : (kZeroRows ? 0.f : rr[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = row_keep ? v[i] : 0.f;
+      }
+      *slot = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tm_out, buf, n0, row0);  // rows >= M are clipped
+      bulk_commit_group();
+    }
+  }
+}
+
 // Epilogue of one output tile for one warp.  t_row = TMEM address of this
 // thread's lane at the accumulator buffer's first column; row0 = first of the
 // warp's 32 output rows; the warp handles columns half `col_half` of
@@ -181,6 +251,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
                                               const CUtensorMap* tm_res, uint32_t t_row, int row0,
                                               int n_blk, int col_half, EpiState& es,
                                               int* status, volatile int* abort_flag) {
+  if constexpr (std::is_same<TOut, float>::value) {
+    epilogue_tile_f32<BN, EPI>(p, tm_out, tm_res, t_row, row0, n_blk, col_half, es, status, abort_flag);
+    return;
+  }
   const int lane = threadIdx.x & 31;
   const int m = row0 + lane;
   const bool row_ok = m < p.M;
@@ -201,7 +275,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
         dst[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]);
     }
     return;
-  } else {
+  } else if constexpr (!std::is_same<TOut, float>::value) {
     constexpr bool kZeroRows = EPI == (int)Epi::kBiasResidualZeroRows;
     constexpr bool kGelu = EPI == (int)Epi::kBiasGelu;
     constexpr bool kResidual =
@@ -296,6 +370,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
 template <typename TIn>
 constexpr CUtensorMapDataType tmap_dtype() {
   return std::is_same<TIn, int8_t>::value    ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+         : std::is_same<TIn, float>::value  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
          : std::is_same<TIn, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
@@ -708,7 +783,8 @@ int make_maps(const GemmArgs& g, int box_a_rows, int box_b_rows, CUtensorMap* ta
     const CUtensorMapDataType odt = tmap_dtype<TOut>();
     const uint64_t dims[2] = {(uint64_t)g.n, (uint64_t)g.m};
     const uint64_t strides[1] = {(uint64_t)g.n * sizeof(TOut)};
-    const uint32_t box[2] = {(uint32_t)kEpiBoxCols, (uint32_t)kEpiBoxRows};
+    // one 128-byte row per box row: 64 16-bit or 32 fp32 columns
+    const uint32_t box[2] = {(uint32_t)(128 / sizeof(TOut)), (uint32_t)kEpiBoxRows};
     if (int rc = encode_tmap(tout, odt, 2, g.out, dims, strides, box)) return rc;
     if (g.residual != nullptr) {
       if (int rc = encode_tmap(tres, odt, 2, g.residual, dims, strides, box)) return rc;
@@ -793,6 +869,17 @@ int dispatch_epi(const GemmArgs& g, cudaStream_t stream) {
   }
 }
 
+// 16-bit operands, fp32 output (bias and residual fp32): the fp32 residual stream.
+template <typename TIn>
+int dispatch_epi_f32(const GemmArgs& g, cudaStream_t stream) {
+  switch (g.epi) {
+    case Epi::kBias: return dispatch_bn<TIn, float, (int)Epi::kBias>(g, stream);
+    case Epi::kBiasResidual: return dispatch_bn<TIn, float, (int)Epi::kBiasResidual>(g, stream);
+    case Epi::kBiasResidualZeroRows: return dispatch_bn<TIn, float, (int)Epi::kBiasResidualZeroRows>(g, stream);
+    default: return fail(TTJ_ERR_INVALID_ARG, "epilogue not valid for fp32 output");
+  }
+}
+
 template <typename TOut>
 int dispatch_int8(const GemmArgs& g, cudaStream_t stream) {
   switch (g.epi) {
@@ -806,6 +893,8 @@ int dispatch_int8(const GemmArgs& g, cudaStream_t stream) {
 }  // namespace
 
 int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
+  if (g.out_dtype == TTJ_F32 && g.in_dtype == TTJ_F16) return dispatch_epi_f32<__half>(g, stream);
+  if (g.out_dtype == TTJ_F32 && g.in_dtype == TTJ_BF16) return dispatch_epi_f32<__nv_bfloat16>(g, stream);
   if (g.in_dtype == TTJ_F16) return dispatch_epi<__half, __half>(g, stream);
   if (g.in_dtype == TTJ_BF16) return dispatch_epi<__nv_bfloat16, __nv_bfloat16>(g, stream);
   // int8 operands

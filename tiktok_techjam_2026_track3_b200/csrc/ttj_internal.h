@@ -112,10 +112,13 @@ int launch_flash_attn(const AttnArgs& a, cudaStream_t stream);
 
 int launch_wait_timeout_selftest(int* status, int64_t limit_us, cudaStream_t stream);
 
-// LayerNorm over rows of length d (d % 8 == 0, d <= 8192); rows with a zero
-// row_mask byte are written as zeros.
+// LayerNorm over rows of length d (d % 8 == 0, d <= 8192; fp32 input: d <= 4096);
+// rows with a zero row_mask byte are written as zeros.  dtype is the input's
+// (and, for 16-bit input, gamma/beta/output's); with dtype TTJ_F32, gamma and
+// beta are fp32 and out_dtype picks the output type (TTJ_F16 / TTJ_BF16 / TTJ_F32).
 int launch_layernorm(const void* x, const void* gamma, const void* beta, const uint8_t* row_mask,
-                     void* y, int64_t rows, int64_t d, float eps, int dtype, cudaStream_t stream);
+                     void* y, int64_t rows, int64_t d, float eps, int dtype, cudaStream_t stream,
+                     int out_dtype = -1);
 
 int launch_quant_rows(const void* x, int8_t* q, float* scale, int64_t rows, int64_t cols,
                       int dtype, cudaStream_t stream);

@@ -205,10 +205,10 @@ def attn_layer(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, w_o: t
 def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
               row_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """nn.LayerNorm over the last dimension (fp32 arithmetic); rows whose mask
-    entry is False come out as zeros."""
+    entry is False come out as zeros.  fp16, bf16 or fp32 (d <= 4096) rows."""
     lib = _lib.load()
     x = _cuda(x, "x")
-    dt = _dtype_code(x)
+    dt = _lib.TTJ_F32 if x.dtype == torch.float32 else _dtype_code(x)
     d = x.shape[-1]
     rows = x.numel() // d
     if weight.dtype != x.dtype or bias.dtype != x.dtype:
@@ -246,6 +246,16 @@ def linear_gelu(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor) -> torch.T
 
 BLOCK_PARAMS = ("ln1_w", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_w", "ln2_b",
                 "w_in", "b_in", "w_out", "b_out")
+# An fp32 block (fp32 residual stream) keeps these in fp32 and the rest in fp16
+# (ttj_transformer_block_fwd with TTJ_F32).
+BLOCK_F32_STREAM_PARAMS = ("ln1_w", "ln1_b", "b_o", "ln2_w", "ln2_b", "b_out")
+
+
+def block_param_dtype(name: str, x_dtype: torch.dtype) -> torch.dtype:
+    """dtype the block kernels expect for parameter `name` given the input dtype."""
+    if x_dtype == torch.float32:
+        return torch.float32 if name in BLOCK_F32_STREAM_PARAMS else torch.float16
+    return x_dtype
 
 
 def transformer_block(x: torch.Tensor, params: Dict[str, torch.Tensor], num_heads: int,
@@ -253,19 +263,22 @@ def transformer_block(x: torch.Tensor, params: Dict[str, torch.Tensor], num_head
                       valid_token_mask: Optional[torch.Tensor] = None,
                       out: Optional[torch.Tensor] = None,
                       workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """One pre-norm block (BaselineTransformerBlock.forward) in six launches;
-    ``params`` holds the tensors named in BLOCK_PARAMS (w_qkv packed q|k|v)."""
+    """One pre-norm block (BaselineTransformerBlock.forward) in seven launches;
+    ``params`` holds the tensors named in BLOCK_PARAMS (w_qkv packed q|k|v) in
+    the dtypes of ``block_param_dtype``: x's dtype for fp16 / bf16 blocks; for
+    fp32 x an fp32 residual stream with fp16 tensor-core operands."""
     lib = _lib.load()
     x = _cuda(x, "x")
-    dt = _dtype_code(x)
+    dt = _lib.TTJ_F32 if x.dtype == torch.float32 else _dtype_code(x)
     if x.dim() != 3:
         raise RuntimeError(f"x must be [B,S,D], got {tuple(x.shape)}")
     B, S, D = x.shape
     ptrs = {}
     for name in BLOCK_PARAMS:
         t = params[name]
-        if t.dtype != x.dtype or t.device != x.device:
-            raise RuntimeError(f"{name} must be {x.dtype} on {x.device}")
+        want = block_param_dtype(name, x.dtype)
+        if t.dtype != want or t.device != x.device:
+            raise RuntimeError(f"{name} must be {want} on {x.device}")
         ptrs[name] = _cuda(t, name).data_ptr()
     F = params["w_in"].shape[0]
     if params["w_in"].shape != (F, D) or params["w_out"].shape != (D, F) or params["w_qkv"].shape != (3 * D, D):

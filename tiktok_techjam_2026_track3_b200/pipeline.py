@@ -22,7 +22,7 @@ from typing import Callable, Iterator, List, Optional, Sequence
 
 import torch
 
-__all__ = ["HostPipeline", "device_numa_node", "near_device"]
+__all__ = ["HostPipeline", "device_local_cpus", "near_device"]
 
 
 def _parse_cpulist(text: str) -> List[int]:
@@ -38,37 +38,49 @@ def _parse_cpulist(text: str) -> List[int]:
     return cpus
 
 
-def device_numa_node(device: torch.device) -> Optional[int]:
-    """NUMA node of the GPU's PCI slot (Linux sysfs), or None if unknown."""
+def device_local_cpus(device: torch.device) -> Optional[List[int]]:
+    """CPUs close to the GPU (NVML's ideal CPU affinity of the device, read only;
+    else the sysfs NUMA node of its PCI slot), or None if unknown."""
     props = torch.cuda.get_device_properties(device)
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        handle = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{props.uuid}")
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        cpus = [64 * w + b for w, mask in enumerate(words) for b in range(64) if (mask >> b) & 1]
+        if cpus:
+            return cpus
+    except Exception:
+        pass
     try:
         addr = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
         with open(f"/sys/bus/pci/devices/{addr}/numa_node") as f:
             node = int(f.read().strip())
+        if node >= 0:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                return _parse_cpulist(f.read())
     except (AttributeError, OSError, ValueError):
-        return None
-    return node if node >= 0 else None
+        pass
+    return None
 
 
 @contextlib.contextmanager
-def near_device(device: torch.device) -> Iterator[Optional[int]]:
-    """Run the body with this process's CPU affinity restricted to the CPUs of
-    the GPU's NUMA node, then restore it.  Pinned host buffers allocated inside
-    get their pages from memory local to that GPU (first touch by a thread on
-    that node), so their PCIe copies do not cross the socket interconnect.
-    Yields the node (None when it cannot be determined; nothing changes then)."""
-    node = device_numa_node(device)
+def near_device(device: torch.device) -> Iterator[Optional[List[int]]]:
+    """Run the body with this process's CPU affinity restricted to the CPUs
+    close to the GPU (``device_local_cpus``), then restore it.  Pinned host
+    buffers allocated inside get their pages from memory local to those CPUs
+    (first touch), so their PCIe copies do not cross the socket interconnect.
+    Yields the CPU list (None when it cannot be determined; nothing changes)."""
+    cpus = device_local_cpus(device)
     old = None
-    if node is not None and hasattr(os, "sched_setaffinity"):
+    if cpus and hasattr(os, "sched_setaffinity"):
         try:
-            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
-                cpus = _parse_cpulist(f.read())
             old = os.sched_getaffinity(0)
             os.sched_setaffinity(0, cpus)
         except OSError:
-            old, node = None, None
+            old, cpus = None, None
     try:
-        yield node
+        yield cpus
     finally:
         if old is not None:
             os.sched_setaffinity(0, old)

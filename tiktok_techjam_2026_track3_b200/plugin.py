@@ -18,11 +18,15 @@ out-proj GEMM with bias + mask + residual, LayerNorm, ffn_in GEMM with bias +
 exact GELU, ffn_out GEMM with bias + residual + the block's row zeroing; the
 final norm and its masked_fill (Ref:169-171) are one LayerNorm launch.
 fp16 / bf16 models run in their own dtype.  fp32 models (the benchmark's
-default dtype) run the same kernels on fp16 copies of the parameters and of
-the input (fp32 accumulation inside every kernel) and return fp32, as the
-reference's own optimised route does for fp32 models
-(Project/submission/dispatcher_region.py:760-801 packs fp16 weights); the GPU
-tests hold the result to the benchmark's tolerance against the fp32 reference.
+default dtype) keep the residual stream, the LayerNorm parameters and the
+residual-side biases in fp32 and run every GEMM and the attention on fp16
+copies of the weights (fp32 accumulation inside every kernel): the LayerNorm
+kernels read the fp32 stream and write fp16 operands, the out-proj and ffn_out
+epilogues add in fp32 and write the fp32 stream.  The reference's own optimised
+route runs fp32 models on fp16 weights too (Project/submission/dispatcher_region.py:760-801),
+with an fp16 stream; measured on the official shapes, an fp16 stream misses
+the benchmark tolerance on a few elements, the fp32 stream meets it (the GPU
+tests hold every shape to it against the fp32 reference).
 
 Repeated calls with the same input shape, dtype, mask presence and weights are
 replayed from a CUDA graph captured on the second such call (the reference's
@@ -43,7 +47,7 @@ import torch.nn as nn
 from . import ops
 from .layer import B200SelfAttention, _version
 
-__all__ = ["make_user_optimized_transformer", "build", "attention_sublayer"]
+__all__ = ["make_user_optimized_transformer", "build", "attention_sublayer", "block_forward"]
 
 _CACHE_ATTR = "_ttj_attention"
 _BLOCK_ATTR = "_ttj_block"
@@ -72,17 +76,15 @@ def attention_sublayer(block: nn.Module) -> B200SelfAttention:
 _GRAPH_MAX_ELEMENTS = 1 << 24
 
 
-def _compute_dtype(dtype: torch.dtype) -> torch.dtype:
-    if dtype in (torch.float16, torch.bfloat16):
-        return dtype
-    if dtype == torch.float32:
-        return torch.float16
-    raise RuntimeError(f"unsupported dtype {dtype}: the sm_100a kernels take float32, float16 or bfloat16 models")
+def _check_dtype(dtype: torch.dtype) -> None:
+    if dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise RuntimeError(f"unsupported dtype {dtype}: the sm_100a kernels take float32, float16 or bfloat16 models")
 
 
 def _block_params(block, dtype: torch.dtype) -> Dict[str, torch.Tensor]:
-    """The block's parameters in the kernels' layout (q|k|v packed) and compute
-    dtype, cached and rebuilt when any parameter's storage or version changes."""
+    """The block's parameters in the kernels' layout (q|k|v packed) and the
+    dtypes ``ops.block_param_dtype`` gives for a `dtype` input, cached and
+    rebuilt when any parameter's storage or version changes."""
     att = block.attention
     src = (block.norm1.weight, block.norm1.bias, att.q_proj.weight, att.q_proj.bias,
            att.k_proj.weight, att.k_proj.bias, att.v_proj.weight, att.v_proj.bias,
@@ -93,15 +95,14 @@ def _block_params(block, dtype: torch.dtype) -> Dict[str, torch.Tensor]:
     if cached is not None and cached[0] == key:
         return cached[1]
     with torch.no_grad():
-        t = [p.detach().to(dtype) for p in src]
+        t = [p.detach() for p in src]
         packed = {
-            "ln1_w": t[0].contiguous(), "ln1_b": t[1].contiguous(),
-            "w_qkv": torch.cat([t[2], t[4], t[6]], 0).contiguous(),
-            "b_qkv": torch.cat([t[3], t[5], t[7]], 0).contiguous(),
-            "w_o": t[8].contiguous(), "b_o": t[9].contiguous(), "ln2_w": t[10].contiguous(),
-            "ln2_b": t[11].contiguous(), "w_in": t[12].contiguous(), "b_in": t[13].contiguous(),
-            "w_out": t[14].contiguous(), "b_out": t[15].contiguous(),
+            "ln1_w": t[0], "ln1_b": t[1],
+            "w_qkv": torch.cat([t[2], t[4], t[6]], 0), "b_qkv": torch.cat([t[3], t[5], t[7]], 0),
+            "w_o": t[8], "b_o": t[9], "ln2_w": t[10], "ln2_b": t[11],
+            "w_in": t[12], "b_in": t[13], "w_out": t[14], "b_out": t[15],
         }
+        packed = {k: v.to(ops.block_param_dtype(k, dtype)).contiguous() for k, v in packed.items()}
     block.__dict__[_BLOCK_ATTR] = (key, packed)
     return packed
 
@@ -118,16 +119,23 @@ def _final_norm_params(model, dtype: torch.dtype) -> Tuple[torch.Tensor, torch.T
     return wb
 
 
+def block_forward(block, x: torch.Tensor, mask: Optional[torch.Tensor], causal: bool) -> torch.Tensor:
+    """One BaselineTransformerBlock.forward (Ref:134-145) as one
+    ttj_transformer_block_fwd call.  fp16 / bf16 x: the block in that dtype;
+    fp32 x: an fp32 residual stream with fp16 tensor-core operands (the
+    block's parameters are converted once and cached)."""
+    return ops.transformer_block(x, _block_params(block, x.dtype), block.attention.num_heads, causal,
+                                 block.norm1.eps, block.norm2.eps, mask)
+
+
 def _model_forward(model, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
-    """Blocks + final norm on the kernels, in the compute dtype of x's dtype."""
-    cdt = _compute_dtype(x.dtype)
-    h = x if x.dtype == cdt else x.to(cdt)
+    """Blocks + final norm on the kernels (residual stream in x's dtype)."""
+    _check_dtype(x.dtype)
+    h = x
     for layer in model.layers:
-        h = ops.transformer_block(h, _block_params(layer, cdt), layer.attention.num_heads,
-                                  model.config.causal, layer.norm1.eps, layer.norm2.eps, mask)
-    w, b = _final_norm_params(model, cdt)
-    out = ops.layernorm(h, w, b, model.final_norm.eps, row_mask=mask)
-    return out if out.dtype == x.dtype else out.to(x.dtype)
+        h = block_forward(layer, h, mask, model.config.causal)
+    w, b = _final_norm_params(model, x.dtype)
+    return ops.layernorm(h, w, b, model.final_norm.eps, row_mask=mask)
 
 
 def _weights_key(model):
