@@ -63,9 +63,6 @@ constexpr uint32_t kRegsSoftmax = 208;
 static_assert(kRegsCtl + 2 * kRegsSoftmax == 3 * kLaunchRegs, "register split must use the launch budget");
 constexpr uint32_t kTmemCols = 512;
 constexpr int64_t kHeadMajorKvBytes = int64_t(96) << 20;
-#ifndef TTJ_PINGPONG
-#define TTJ_PINGPONG 1
-#endif
 
 struct AttnParams {
   void* ctx;
@@ -527,7 +524,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
     // head_dim 64 (cfg2 shapes: non-causal 226 -> 214 us, B4 S8192 causal
     // ~5% faster, cfg2 causal unchanged); at head_dim 128, where the next S of
     // a tile waits for its own P.V, it measured 2% slower.
-    constexpr bool kTurns = TTJ_PINGPONG && HD == 64;
+    constexpr bool kTurns = HD == 64;
     uint32_t turn_ph = 0;
     auto take_turn = [&]() -> bool {
       const bool got = mbar_wait_warp(&turn[t * 4 + lg], turn_ph, p.status, kDevTimeoutSoftmax, abort_flag);
