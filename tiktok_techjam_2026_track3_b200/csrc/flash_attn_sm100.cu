@@ -519,11 +519,15 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
     // exponentials keep the MUFU pipe busy.  Measured: one warp alone drives
     // the exponential unit at ~84% of its rate, two at ~97%; without turns the
     // two tiles fall into step (both exponentiate, then both leave the unit
-    // idle).  Tile A passes a turn without exponentials for each key tile only
-    // tile B has (causal items), so the two sequences stay aligned.  Used at
-    // head_dim 64 (cfg2 shapes: non-causal 226 -> 214 us, B4 S8192 causal
-    // ~5% faster, cfg2 causal unchanged); at head_dim 128, where the next S of
-    // a tile waits for its own P.V, it measured 2% slower.
+    // idle).  Turns are taken on an item's interior key tiles only, j in
+    // [1, n_A - 1) for both tiles (n_A = tile A's key-tile count), so both
+    // take the same number and the sequences stay aligned; an item's first and
+    // last steps run free, so a tile waiting for its last P.V or storing its
+    // context never holds up the other tile's exponentials (with turns on every
+    // step, tile A waited ~3,000 cycles per causal item).  Used at head_dim 64
+    // (cfg2 shapes: non-causal 226 -> 214 us, B4 S8192 causal ~5% faster); at
+    // head_dim 128, where the next S of a tile waits for its own P.V, turns
+    // measured 2% slower.
     constexpr bool kTurns = HD == 64;
     uint32_t turn_ph = 0;
     auto take_turn = [&]() -> bool {
@@ -541,6 +545,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       if (item >= p.num_items) break;
       const Item it = decode_item<CAUSAL>(item, p);
       const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
+      const int n_turn_end = kv_tiles<CAUSAL, NT>(it.pair, 0, p.S);  // turns on steps [1, n_A - 1)
       const int q0 = it.pair * NT * kBM + t * kBM;
       const int q_row = q0 + r;
       const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
@@ -644,7 +649,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         // row sums as fp32 pairs in four chains.
         uint32_t pk[2][32];
         uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-        if (kTurns && !take_turn()) { ok = false; break; }
+        const bool turn_step = kTurns && j >= 1 && j + 1 < n_turn_end;
+        if (turn_step && !take_turn()) { ok = false; break; }
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) {
           uint32_t (&pc)[16] = *reinterpret_cast<uint32_t(*)[16]>(&pk[c >> 1][(c & 1) * 16]);
@@ -660,7 +666,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           }
           if constexpr (!kSepP) tmem_st16(t_p + c * 16, pc);
         }
-        if (kTurns) pass_turn();
+        if (turn_step) pass_turn();
         float a0, a1;
         f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), a0, a1);
         const float sum = a0 + a1;
@@ -694,13 +700,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      if (kTurns && t == 0) {  // tile B's extra key tile of a causal item: pass its turn
-        for (int e = n_kv; e < kv_tiles<CAUSAL, NT>(it.pair, 1, p.S); ++e) {
-          if (!take_turn()) { ok = false; break; }
-          pass_turn();
-        }
-        if (!ok) break;
-      }
       // epilogue: wait for the last P.V, then O_t / l -> ctx rows (heads merged)
       if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) break;
       od_phase ^= 1u;
