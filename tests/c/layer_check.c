@@ -205,5 +205,8 @@ int main(void) {
   fails += run_case(2, 100, 128, 2, 1, 0, 1234);  /* head_dim 64, causal, ragged S */
   fails += run_case(2, 130, 128, 2, 0, 1, 1235);  /* head_dim 64, key padding mask */
   fails += run_case(1, 200, 256, 2, 1, 1, 1236);  /* head_dim 128, causal + mask */
+  fails += run_case(3, 128, 128, 4, 1, 0, 1237);  /* head_dim 32 (the reference's shapes 1-6, 12, 13) */
+  fails += run_case(2, 90, 32, 4, 1, 1, 1238);    /* head_dim 8, d_model 32 (shape 7), ragged + mask */
+  fails += run_case(2, 140, 512, 2, 1, 0, 1239);  /* head_dim 256 (shape 8), ragged S */
   return fails == 0 ? 0 : 1;
 }

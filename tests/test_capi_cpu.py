@@ -116,6 +116,16 @@ def test_argument_validation_without_device():
     b.workspace_bytes = 1 << 40
     b.out = b.x
     assert lib.ttj_transformer_block_fwd(C.byref(b), None) == -1
+    # fp32 residual stream (TTJ_F32): accepted by the block and LayerNorm only, d <= 4096
+    b.out = fake * 2
+    b.dtype = 2
+    b.d_model, b.num_heads = 8192, 64
+    assert lib.ttj_transformer_block_fwd(C.byref(b), None) == -2
+    assert b"4096" in lib.ttj_last_error()
+    assert lib.ttj_layernorm_fwd(fake, fake, fake, None, fake, 4, 8192, 1e-5, 2, None) == -2
+    assert lib.ttj_layernorm_fwd(fake, fake, fake, None, fake, 4, 12, 1e-5, 2, None) == -2
+    assert lib.ttj_linear_fwd(fake, fake, fake, None, None, fake, 4, 32, 8, 2, None, None) == -1
+    assert lib.ttj_flash_attn_fwd(fake, None, fake, 1, 16, 2, 64, 1, 2, None, None) == -1
 
 
 def test_workspace_sizes():
@@ -127,6 +137,8 @@ def test_workspace_sizes():
     # block: norm output, max(3D, F) wide buffer, context, x1
     assert lib.ttj_block_workspace_size(8, 2048, 1024, 4096, 0) == t * d * 2 * 3 + t * 4096 * 2
     assert lib.ttj_block_workspace_size(8, 2048, 1024, 1024, 0) == t * d * 2 * 3 + t * 3 * d * 2
+    # fp32 residual stream: x1 is fp32
+    assert lib.ttj_block_workspace_size(8, 2048, 1024, 4096, 2) == t * d * 2 * 2 + t * d * 4 + t * 4096 * 2
 
 
 def test_missing_library_fails_loudly(tmp_path):

@@ -20,4 +20,4 @@ def test_c_program_layer_matches_reference(tmp_path):
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
     outside = [int(m) for m in re.findall(r"(\d+) of \d+ outside the predicate", res.stdout)]
-    assert outside == [0, 0, 0], res.stdout
+    assert outside == [0] * 6, res.stdout

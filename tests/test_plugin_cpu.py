@@ -44,3 +44,15 @@ def test_official_shapes_table_matches_reference_manifest():
         assert (m.batch, m.d_model, m.num_heads, m.seq_len, m.num_layers, m.ffn_dim, m.causal) == (
             s["batch_size"], s["d_model"], s["num_heads"], s["seq_len"], s["num_layers"], s["ffn_dim"],
             s["causal"])
+
+
+def test_block_parameter_dtypes_for_each_model_dtype():
+    """16-bit models keep every block parameter in their dtype; fp32 models keep the
+    LayerNorm parameters and the residual-side biases in fp32 (the fp32 residual
+    stream) and the tensor-core operands in fp16."""
+    from tiktok_techjam_2026_track3_b200 import ops
+    for dt in (torch.float16, torch.bfloat16):
+        assert all(ops.block_param_dtype(n, dt) == dt for n in ops.BLOCK_PARAMS)
+    f32 = {n for n in ops.BLOCK_PARAMS if ops.block_param_dtype(n, torch.float32) == torch.float32}
+    assert f32 == {"ln1_w", "ln1_b", "b_o", "ln2_w", "ln2_b", "b_out"}
+    assert all(ops.block_param_dtype(n, torch.float32) == torch.float16 for n in ops.BLOCK_PARAMS if n not in f32)
