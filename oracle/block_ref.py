@@ -20,7 +20,7 @@ import torch.nn.functional as F
 from .attention_ref import LayerWeights, attention_layer_ref
 
 __all__ = ["TransformerConfigRef", "BaselineSelfAttentionRef", "BaselineTransformerBlockRef",
-           "BaselineTransformerRef"]
+           "BaselineTransformerRef", "streamed_model_ref"]
 
 
 @dataclass(frozen=True)
@@ -132,3 +132,88 @@ class BaselineTransformerRef(nn.Module):
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x
+
+
+def _streamed_heads_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                              causal: bool, key_mask: Optional[torch.Tensor],
+                              q_chunk: int, k_chunk: int) -> torch.Tensor:
+    """softmax(q k^T * scale + masks) v for one batch row, all heads at once
+    ([H,S,hd] each), in fp32 over (query chunk x key chunk) blocks with a
+    running max and sum: the S x S table never exists.  Causal query chunks
+    stop at their last row's key.  Rows that see no key (possible only with a
+    key mask) come out as zeros."""
+    H, S, hd = q.shape
+    out = torch.empty_like(q)
+    for qs in range(0, S, q_chunk):
+        qe = min(qs + q_chunk, S)
+        run_max = torch.full((H, qe - qs), float("-inf"), device=q.device)
+        run_sum = torch.zeros(H, qe - qs, device=q.device)
+        acc = torch.zeros(H, qe - qs, hd, device=q.device)
+        qidx = torch.arange(qs, qe, device=q.device)
+        for ks in range(0, qe if causal else S, k_chunk):
+            ke = min(ks + k_chunk, qe if causal else S)
+            s = torch.matmul(q[:, qs:qe], k[:, ks:ke].transpose(1, 2)).mul_(scale)
+            kidx = torch.arange(ks, ke, device=q.device)
+            if causal and ke - 1 > qs:
+                s.masked_fill_((kidx[None, :] > qidx[:, None])[None], float("-inf"))
+            if key_mask is not None:
+                s.masked_fill_(~key_mask[ks:ke][None, None, :], float("-inf"))
+            new_max = torch.maximum(run_max, s.amax(dim=2))
+            safe = torch.where(torch.isinf(new_max), torch.zeros_like(new_max), new_max)
+            alpha = torch.exp(run_max - safe)
+            p = s.sub_(safe[..., None]).exp_()
+            run_sum = run_sum * alpha + p.sum(dim=2)
+            acc = acc * alpha[..., None] + torch.matmul(p, v[:, ks:ke])
+            run_max = new_max
+            del s, p
+        out[:, qs:qe] = acc / torch.where(run_sum > 0, run_sum, torch.ones_like(run_sum))[..., None]
+    return out
+
+
+def streamed_model_ref(model: "BaselineTransformerRef", x: torch.Tensor,
+                       valid_token_mask: Optional[torch.Tensor] = None,
+                       q_chunk: int = 4096, k_chunk: int = 16384) -> torch.Tensor:
+    """``BaselineTransformer.forward`` (Ref:148-172, blocks Ref:125-145) in fp32
+    for sequences whose score table cannot be held (the reference's official
+    shape 14, S = 100000): the model's own LayerNorms, projections, exact-erf
+    FFN and final norm, with each attention evaluated over (query chunk x key
+    chunk) blocks with a running max and sum.  That is the behaviour of the
+    reference's long-context checker (Project/tools/shape14_eval.py:201-254,
+    which swaps ``attention.forward`` for a streamed version); here all heads
+    of a batch row go through each block together.  Batch rows are evaluated
+    one at a time, on x's device; returns fp32 [B,S,D]."""
+    cfg = model.config
+    B, S, D = x.shape
+    H = cfg.num_heads
+    hd = D // H
+    out = torch.empty(B, S, D, device=x.device)
+
+    def lin(t, m):
+        return F.linear(t, m.weight.float(), m.bias.float())
+
+    def norm(t, m):
+        return F.layer_norm(t, (D,), m.weight.float(), m.bias.float(), m.eps)
+
+    for b in range(B):
+        h = x[b].float()
+        km = None if valid_token_mask is None else valid_token_mask[b].to(x.device)
+        for layer in model.layers:
+            att = layer.attention
+            a = norm(h, layer.norm1)
+            q, k, v = (lin(a, m).view(S, H, hd).transpose(0, 1).contiguous()
+                       for m in (att.q_proj, att.k_proj, att.v_proj))
+            ctx = _streamed_heads_attention(q, k, v, hd ** -0.5, cfg.causal, km, q_chunk, k_chunk)
+            del q, k, v
+            o = lin(ctx.transpose(0, 1).reshape(S, D), att.out_proj)           # Ref:113-118
+            if km is not None:
+                o = o.masked_fill(~km[:, None], 0)                              # Ref:120-121
+            h = h + o                                                           # Ref:140
+            f = lin(F.gelu(lin(norm(h, layer.norm2), layer.ffn_in), approximate="none"), layer.ffn_out)
+            h = h + f                                                           # Ref:141-142
+            if km is not None:
+                h = h.masked_fill(~km[:, None], 0)                              # Ref:143-144
+        h = norm(h, model.final_norm)                                           # Ref:168
+        if km is not None:
+            h = h.masked_fill(~km[:, None], 0)                                  # Ref:170-171
+        out[b] = h
+    return out

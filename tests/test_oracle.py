@@ -144,54 +144,43 @@ def test_block_oracle_matches_reference_model(golden_dir):
     torch.testing.assert_close(out, fx["out"], rtol=1e-5, atol=1e-5)
 
 
-def _streamed_model(model):
-    """The model with every block's attention evaluated by the streamed checker,
-    per (batch, head), 512-key chunks (no S x S table): the substitution the
-    reference makes to check sequences whose dense scores do not fit
-    (Project/tools/shape14_eval.py:201-254)."""
-    import types
-
-    def fwd(self, x, valid_token_mask=None, causal=False, in_dtype=False):
-        B, S, D = x.shape
-        H = self.num_heads
-        q, k, v = (split_heads(torch.nn.functional.linear(x, m.weight, m.bias), H)
-                   for m in (self.q_proj, self.k_proj, self.v_proj))
-        ctx = torch.empty_like(q)
-        for b in range(B):
-            km = None if valid_token_mask is None else valid_token_mask[b]
-            for h in range(H):
-                ctx[b, h] = streamed_attention_ref(q[b, h], k[b, h], v[b, h], (D // H) ** -0.5, causal,
-                                                   key_mask=km, k_chunk=512)
-        out = torch.nn.functional.linear(ctx.transpose(1, 2).reshape(B, S, D), self.out_proj.weight,
-                                         self.out_proj.bias)
-        if valid_token_mask is not None:
-            out = out.masked_fill(~valid_token_mask[..., None], 0)
-        return out
-
-    for layer in model.layers:
-        layer.attention.forward = types.MethodType(fwd, layer.attention)
-    return model
-
-
 @pytest.mark.parametrize("seq,batch", [(1024, 2), (2048, 2), (4096, 1)])
 def test_streamed_checker_gate_whole_model(seq, batch):
     """The reference's own gate for its long-context checker
-    (Project/tools/shape14_eval.py:279-316): the whole model (d_model 1024,
-    16 heads, ffn 1024, 2 layers, causal) with streamed attention against the
-    dense model, S in {1024, 2048, 4096}, three seeds each, max |diff| < 1e-3 in
-    fp32."""
-    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef
+    (Project/tools/shape14_eval.py:279-316): the whole model of official shape
+    14 (d_model 1024, 16 heads, ffn 1024, 2 layers, causal) evaluated by
+    ``streamed_model_ref`` against the dense model, S in {1024, 2048, 4096},
+    three seeds each, max |diff| < 1e-3 in fp32.  The chunk sizes divide
+    neither S nor each other, so ragged query and key chunks are exercised."""
+    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef, streamed_model_ref
     cfg = TransformerConfigRef(batch_size=batch, seq_len=seq, d_model=1024, num_heads=16, ffn_dim=1024,
                                num_layers=2, causal=True)
     torch.manual_seed(seq)
     dense = BaselineTransformerRef(cfg).eval()
-    streamed = _streamed_model(BaselineTransformerRef(cfg).eval())
-    streamed.load_state_dict(dense.state_dict())
     for seed in (1234, 1235, 1236):
         x, mask = generate_case(batch, seq, 1024, seed)
         with torch.inference_mode():
-            err = (streamed(x, mask) - dense(x, mask)).abs().max().item()
+            err = (streamed_model_ref(dense, x, mask, q_chunk=700, k_chunk=1100) - dense(x, mask)).abs().max().item()
         assert err < 1e-3, (seq, seed, err)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_streamed_model_with_padding_and_small_chunks(causal):
+    """``streamed_model_ref`` with prefix key masks (padded rows zeroed, the
+    reference's generator at padding 0.4) and chunks of a few rows, against the
+    dense model to 1e-5."""
+    from oracle.block_ref import BaselineTransformerRef, TransformerConfigRef, streamed_model_ref
+    cfg = TransformerConfigRef(batch_size=3, seq_len=200, d_model=64, num_heads=4, ffn_dim=96,
+                               num_layers=2, causal=causal)
+    torch.manual_seed(7)
+    dense = BaselineTransformerRef(cfg).eval()
+    x, mask = generate_case(3, 200, 64, 1240, padding_ratio=0.4)
+    assert not bool(mask.all())
+    with torch.inference_mode():
+        ref = dense(x, mask)
+        got = streamed_model_ref(dense, x, mask, q_chunk=37, k_chunk=23)
+    torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
+    assert bool((got[~mask] == 0).all())
 
 
 def test_rows_ref_matches_dense_layer_and_rounding_points():
