@@ -75,6 +75,28 @@ struct EpiState {
   uint64_t* bar1;
   uint32_t phase0, phase1;
   int next;            // buffer to use next
+  int pending;         // the residual box of this warp's first chunk is already requested
+};
+
+// Hands a tile's TMEM accumulator back to the MMA thread once this warp has
+// read its part of it (one arrival per epilogue warp and tile), before the
+// warp's stores: on this CTA's barrier, or on the pair leader's (cluster
+// address) for a CTA pair.  arrive() is idempotent, so every exit path of an
+// epilogue can end with it.
+struct AccRelease {
+  uint64_t* local;   // this CTA's barrier, or null
+  uint32_t remote;   // shared::cluster address of the leader's barrier (local == null)
+  bool done;
+  __device__ __forceinline__ void arrive() {
+    if (done) return;
+    tc_fence_before();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+      if (local != nullptr) mbar_arrive(local);
+      else mbar_arrive_cluster(remote);
+    }
+    done = true;
+  }
 };
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk16) {
@@ -181,7 +203,7 @@ __device__ __forceinline__ void gelu_erf_pair(float& v0, float& v1) {
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile_f32(const GemmParams& p, const CUtensorMap* tm_out,
                                                   const CUtensorMap* tm_res, uint32_t t_row, int row0,
-                                                  int n_blk, int col_half, EpiState& es,
+                                                  int n_blk, int col_half, EpiState& es, AccRelease& rel,
                                                   int* status, volatile int* abort_flag) {
   constexpr bool kZeroRows = EPI == (int)Epi::kBiasResidualZeroRows;
   constexpr bool kResidual = EPI == (int)Epi::kBiasResidual || kZeroRows;
@@ -211,28 +233,37 @@ __device__ __forceinline__ void epilogue_tile_f32(const GemmParams& p, const CUt
     }
     uint32_t r[32];
     tmem_ld32(t_row + c * 32, r);  // warp-collective
+    if (cc == kChunks - 1) rel.arrive();  // the accumulator is in registers
+    // Every load of the chunk is issued before any arithmetic (16-byte slot q:
+    // columns n0 + 4q .. +3; N % 32 == 0, so all valid).
+    float4 bias[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      bias[q] = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + n0 + 4 * q));
+    float4 res[8];
     if constexpr (kResidual) {
       const uint32_t ph = b ? es.phase1 : es.phase0;
       if (!mbar_wait_warp<true>(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
       if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) res[q] = *reinterpret_cast<const float4*>(buf + swz(lane, q));
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {  // 16-byte slot q: columns n0 + 4q .. +3 (N % 32 == 0: all valid)
-      const float4 bias = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + n0 + 4 * q));
-      float v[4] = {__uint_as_float(r[4 * q]) + bias.x, __uint_as_float(r[4 * q + 1]) + bias.y,
-                    __uint_as_float(r[4 * q + 2]) + bias.z, __uint_as_float(r[4 * q + 3]) + bias.w};
-      float4* slot = reinterpret_cast<float4*>(buf + swz(lane, q));
+    for (int q = 0; q < 8; ++q) {
+      float v[4] = {__uint_as_float(r[4 * q]) + bias[q].x, __uint_as_float(r[4 * q + 1]) + bias[q].y,
+                    __uint_as_float(r[4 * q + 2]) + bias[q].z, __uint_as_float(r[4 * q + 3]) + bias[q].w};
       if constexpr (kResidual) {
-        const float4 res = *slot;
-        const float rr[4] = {res.x, res.y, res.z, res.w};
+        const float rr[4] = {res[q].x, res[q].y, res[q].z, res[q].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = row_keep ? rr[i] + v[i] : (kZeroRows ? 0.f : rr[i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = row_keep ? v[i] : 0.f;
       }
-      *slot = make_float4(v[0], v[1], v[2], v[3]);
+      res[q] = make_float4(v[0], v[1], v[2], v[3]);
     }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) *reinterpret_cast<float4*>(buf + swz(lane, q)) = res[q];
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
@@ -245,14 +276,23 @@ __device__ __forceinline__ void epilogue_tile_f32(const GemmParams& p, const CUt
 // Epilogue of one output tile for one warp.  t_row = TMEM address of this
 // thread's lane at the accumulator buffer's first column; row0 = first of the
 // warp's 32 output rows; the warp handles columns half `col_half` of
-// [n_blk*BN, n_blk*BN + BN).
+// [n_blk*BN, n_blk*BN + BN).  `rel` hands the accumulator back as soon as the
+// warp's last TMEM load has completed.  next_row0 / next_n_blk locate the
+// warp's part of its next tile (next_row0 < 0: none): with a residual and one
+// staging buffer, that tile's first residual box is requested at the end of
+// this one, so it arrives while the next accumulator is still being computed.
+// Measured (cfg2 out-proj, 16384 x 1024 -> 1024 + residual, in the layer):
+// 41.0 -> 37-38 us, same output bits; per %globaltimer stamps, the residual
+// box used to arrive ~1 us after its request and the accumulator was held
+// through the stores.
 template <typename TOut, int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tm_out,
                                               const CUtensorMap* tm_res, uint32_t t_row, int row0,
-                                              int n_blk, int col_half, EpiState& es,
-                                              int* status, volatile int* abort_flag) {
+                                              int n_blk, int col_half, EpiState& es, AccRelease& rel,
+                                              int* status, volatile int* abort_flag,
+                                              int next_row0, int next_n_blk) {
   if constexpr (std::is_same<TOut, float>::value) {
-    epilogue_tile_f32<BN, EPI>(p, tm_out, tm_res, t_row, row0, n_blk, col_half, es, status, abort_flag);
+    epilogue_tile_f32<BN, EPI>(p, tm_out, tm_res, t_row, row0, n_blk, col_half, es, rel, status, abort_flag);
     return;
   }
   const int lane = threadIdx.x & 31;
@@ -268,6 +308,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       const int n0 = n_blk * BN + c * 32;
       uint32_t r[32];
       tmem_ld32(t_row + c * 32, r);
+      if (cc == kChunks - 1) rel.arrive();
       if (!row_ok || n0 >= p.N) continue;
       int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(p.out) + (int64_t)m * p.N + n0);
 #pragma unroll
@@ -299,28 +340,67 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       __syncwarp();
       if (n0 >= p.N) continue;  // whole chunk past the last column (uniform)
       if constexpr (kResidual) {
-        if (lane == 0) {
+        if (lane == 0 && !(cc == 0 && es.pending)) {
           mbar_arrive_expect_tx(bar, kEpiBoxBytes);
           tma_load_2d(buf, tm_res, bar, n0, row0);
         }
+        if (cc == 0) es.pending = 0;
       }
       uint32_t r[64];
       tmem_ld64(t_row + c * kEpiBoxCols, r);  // warp-collective
-      if constexpr (kResidual) {
-        const uint32_t ph = b ? es.phase1 : es.phase0;
-        if (!mbar_wait_warp<true>(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
-        if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
-      }
+      if (cc == kChunks - 1) rel.arrive();     // the accumulator is in registers
+      if constexpr (!kDequant) {
+        // Every load of the chunk before any arithmetic: bias (8 columns per
+        // 16-byte word), then the residual box from shared memory.
+        uint4 bw[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int col = n0 + 8 * j;
-        float v[8];
-        if constexpr (!kDequant) {
-          float bias[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (col < p.N) unpack8<TOut>(__ldg(reinterpret_cast<const uint4*>(static_cast<const TOut*>(p.bias) + col)), bias);
+        for (int j = 0; j < 8; ++j) {
+          const int col = n0 + 8 * j;
+          bw[j] = col < p.N ? __ldg(reinterpret_cast<const uint4*>(static_cast<const TOut*>(p.bias) + col))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        }
+        uint4 w[8];
+        if constexpr (kResidual) {
+          const uint32_t ph = b ? es.phase1 : es.phase0;
+          if (!mbar_wait_warp<true>(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
+          if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j] = *reinterpret_cast<const uint4*>(buf + swz(lane, j));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float v[8], bias[8];
+          unpack8<TOut>(bw[j], bias);
 #pragma unroll
           for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * j + i]) + bias[i];
-        } else {
+          if constexpr (kResidual) {
+            float res[8];
+            unpack8<TOut>(w[j], res);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = row_keep ? res[i] + v[i] : (kZeroRows ? 0.f : res[i]);
+          } else if constexpr (kGelu) {
+            // Exact (erf) GELU of the biased product (gelu_erf_pair above).
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) gelu_erf_pair(v[i], v[i + 1]);
+          } else {
+            // Output-row masking without a residual (the reference's masked_fill
+            // of the attention output, torch_transformer_benchmark.py:120-121).
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = row_keep ? v[i] : 0.f;
+          }
+          w[j] = pack8<TOut>(v);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + swz(lane, j)) = w[j];
+      } else {
+        if constexpr (kResidual) {
+          const uint32_t ph = b ? es.phase1 : es.phase0;
+          if (!mbar_wait_warp<true>(bar, ph, status, kDevTimeoutTmaFull, abort_flag)) return;
+          if (b) es.phase1 ^= 1u; else es.phase0 ^= 1u;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = n0 + 8 * j;
           // k008 recipe order: acc * (s_a * s_w) + bias, each step rounded.
           float ss[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           float bs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -333,35 +413,45 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
             bs[0] = b0.x; bs[1] = b0.y; bs[2] = b0.z; bs[3] = b0.w;
             bs[4] = b1.x; bs[5] = b1.y; bs[6] = b1.z; bs[7] = b1.w;
           }
+          float v[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float acc_f = static_cast<float>(static_cast<int32_t>(r[8 * j + i]));
             v[i] = __fadd_rn(__fmul_rn(acc_f, __fmul_rn(row_scale, ss[i])), bs[i]);
           }
+          uint4* slot = reinterpret_cast<uint4*>(buf + swz(lane, j));
+          if constexpr (kResidual) {
+            float res[8];
+            unpack8<TOut>(*slot, res);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = row_keep ? res[i] + v[i] : res[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = row_keep ? v[i] : 0.f;
+          }
+          *slot = pack8<TOut>(v);
         }
-        uint4* slot = reinterpret_cast<uint4*>(buf + swz(lane, j));
-        if constexpr (kResidual) {
-          float res[8];
-          unpack8<TOut>(*slot, res);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = row_keep ? res[i] + v[i] : (kZeroRows ? 0.f : res[i]);
-        } else if constexpr (kGelu) {
-          // Exact (erf) GELU of the biased product (gelu_erf_pair above).
-#pragma unroll
-          for (int i = 0; i < 8; i += 2) gelu_erf_pair(v[i], v[i + 1]);
-        } else {
-          // Output-row masking without a residual (the reference's masked_fill
-          // of the attention output, torch_transformer_benchmark.py:120-121).
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = row_keep ? v[i] : 0.f;
-        }
-        *slot = pack8<TOut>(v);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         tma_store_2d(tm_out, buf, n0, row0);  // rows >= M / cols >= N are clipped
         bulk_commit_group();
+      }
+    }
+    if constexpr (kResidual && kEpiBufs == 1) {
+      // Request the next tile's first residual box into the (only) buffer once
+      // the last store has read it.
+      const int nn0 = next_n_blk * BN + col_half * kChunks * kEpiBoxCols;
+      if (next_row0 >= 0 && next_row0 < p.M && nn0 < p.N) {
+        rel.arrive();
+        if (lane == 0) {
+          bulk_wait_group_read<0>();
+          mbar_arrive_expect_tx(es.bar0, kEpiBoxBytes);
+          tma_load_2d(es.buf0, tm_res, es.bar0, nn0, next_row0);
+        }
+        es.pending = 1;
+        __syncwarp();
       }
     }
   }
@@ -383,6 +473,7 @@ __device__ __forceinline__ void init_epi_state(EpiState& es, uint8_t* epi_base, 
   es.bar1 = es.bar0 + (kEpiBufs - 1);
   es.phase0 = es.phase1 = 0u;
   es.next = 0;
+  es.pending = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -541,13 +632,17 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc_fence_after();
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;
+      const int nt = tile + (int)gridDim.x;
+      const int nm = nt / p.num_n_blocks;
+      AccRelease rel{&acc_empty[acc], 0u, false};
       epilogue_tile<TOut, BN, EPI>(p, &tmOut, &tmRes,
                                    tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * BN,
-                                   m_blk * kBM + lane_grp * 32, n_blk, col_half, es, p.status, abort_flag);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                                   m_blk * kBM + lane_grp * 32, n_blk, col_half, es, rel, p.status, abort_flag,
+                                   nt < num_tiles ? nm * kBM + lane_grp * 32 : -1, nt - nm * p.num_n_blocks);
+      rel.arrive();
     }
+    // A next-tile residual box still in flight (only after an abort) lands before exit.
+    if (es.pending) mbar_wait_warp<true>(es.bar0, es.phase0, p.status, kDevTimeoutTmaFull, nullptr);
     if (lane == 0) bulk_wait_group_all();
   }
 
@@ -732,14 +827,19 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       tc_fence_after();
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;
+      const int nt = tile + num_pairs;
+      const int nm = nt / p.num_n_blocks;
+      AccRelease rel{nullptr, mapa_shared(smem_u32(&acc_empty[acc]), 0), false};
       epilogue_tile<TOut, BN, EPI>(p, &tmOut, &tmRes,
                                    tmem_base + (static_cast<uint32_t>(lane_grp * 32) << 16) + acc * BN,
-                                   m_blk * 2 * kBM + (int)rank * kBM + lane_grp * 32, n_blk, col_half, es,
-                                   p.status, abort_flag);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+                                   m_blk * 2 * kBM + (int)rank * kBM + lane_grp * 32, n_blk, col_half, es, rel,
+                                   p.status, abort_flag,
+                                   nt < num_tiles ? nm * 2 * kBM + (int)rank * kBM + lane_grp * 32 : -1,
+                                   nt - nm * p.num_n_blocks);
+      rel.arrive();
     }
+    // A next-tile residual box still in flight (only after an abort) lands before exit.
+    if (es.pending) mbar_wait_warp<true>(es.bar0, es.phase0, p.status, kDevTimeoutTmaFull, nullptr);
     if (lane == 0) bulk_wait_group_all();
   }
 
