@@ -685,6 +685,24 @@ def run_ours(args, cfg):
     e2e_ms = max_over_ranks(p0.elapsed_time(p1), world)
     e2e_value = world * T * args.steps / (e2e_ms / 1e3)
 
+    # ---- the copies alone through the same pipeline, a device-side clone of
+    # the input standing in for the layer (a fresh output per step, as the
+    # layer's): the host-link ceiling of the e2e leg on this box, measured the
+    # same way.
+    copies = HostPipeline(lambda xd: xd.clone(), dev, depth=2)
+    with torch.inference_mode():
+        copies.run([x_host] * max(3, args.warmup), [outs_host[i % 2] for i in range(max(3, args.warmup))])
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        copies.run([x_host] * args.steps, [outs_host[i % 2] for i in range(args.steps)])
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    copies_ms = max_over_ranks(c0.elapsed_time(c1), world)
+    copies_value = world * T * args.steps / (copies_ms / 1e3)
+
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -707,6 +725,8 @@ def run_ours(args, cfg):
                 "d2h_bytes_per_step": nbytes,
                 "mode": "B200AttentionLayer calls through HostPipeline (copies of steps i+1 / i-1 overlap step i)",
                 "serial_value": e2e_serial,
+                "copies_only_value": copies_value,
+                "frac_of_copies_only": e2e_value / copies_value,
                 "pinned_near_cpus": None if local_cpus is None else f"{len(local_cpus)} CPUs ({local_cpus[0]}-{local_cpus[-1]})"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
