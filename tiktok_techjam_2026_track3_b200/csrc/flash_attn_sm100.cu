@@ -14,17 +14,20 @@
 // holds one S and one 256-column O per tile).  One CTA per SM loops over work
 // items, heaviest (longest causal key range) first.
 //
-// Roles (384 threads = 12 warps = 3 warpgroups):
+// Roles (head_dim 128 / 256: 384 threads = 3 warpgroups; head_dim 64: 640 = 5):
 //   warp 0       TMA: K_j / V_j tiles into KV_STAGES-deep rings, item after item
 //   warps 1, 3   MMA issue, one thread: S_t = Q_t K_j^T into TMEM, O_t += P_t V_j
 //                with P read from TMEM (tcgen05 "ts" form); head_dim 64: warp 1
 //                for tile A, warp 3 for tile B; head_dim 128: warp 1 for both
 //   warp 2       TMA: the two Q tiles of each work item
-//   warps 4..7   softmax for tile A, warps 8..11 for tile B: thread = query row;
-//                load the S row from TMEM, mask, online softmax in fp32 with a
-//                lazily moved row max, write P (input dtype) to TMEM, rescale its
-//                O row when the max moved, and at the end normalise O and store
-//                the context row at the head's columns of ctx[B,S,D] (head merge).
+//   softmax      head_dim 128 / 256: warps 4..7 for tile A, 8..11 for tile B,
+//                thread = query row; head_dim 64: warps 4..11 for tile A,
+//                12..19 for tile B, two warps per TMEM lane quarter, each with
+//                16 rows (softmax_split below).  Load S from TMEM, mask, online
+//                softmax in fp32 with a lazily moved row max, write P (input
+//                dtype) to TMEM, rescale O when the max moved, and at the end
+//                normalise O and store the context rows at the head's columns
+//                of ctx[B,S,D] (head merge).
 //
 // Two schedules, chosen by what fits in the 512 TMEM columns:
 //
@@ -53,14 +56,6 @@ namespace {
 constexpr int kBM = 128;     // queries per tile
 constexpr int kBN = 128;     // keys per KV tile
 constexpr int kChunkBytes = 128 * 128;  // one [128 rows][64 cols] 16-bit swizzled box
-constexpr int kThreads = 384;
-// Register split (setmaxnreg): the block launches with kLaunchRegs per thread;
-// the first warpgroup (producers, MMA issuer) gives registers back to the two
-// softmax warpgroups.  128 * (kRegsCtl + 2 * kRegsSoftmax) == 384 * kLaunchRegs.
-constexpr int kLaunchRegs = 168;
-constexpr uint32_t kRegsCtl = 88;
-constexpr uint32_t kRegsSoftmax = 208;
-static_assert(kRegsCtl + 2 * kRegsSoftmax == 3 * kLaunchRegs, "register split must use the launch budget");
 constexpr uint32_t kTmemCols = 512;
 constexpr int64_t kHeadMajorKvBytes = int64_t(96) << 20;
 
@@ -81,6 +76,20 @@ struct AttnSmem {
   static_assert(HD == 64 || HD == 128 || HD == 256, "padded head sizes");
   static constexpr int kNT = HD == 256 ? 1 : 2;     // query tiles per work item
   static constexpr bool kSepP = HD == 64;           // separate P buffers in TMEM
+  // head_dim 64: two softmax warps per tile on each SM sub-partition, each
+  // owning 16 of the quarter's 32 rows (16-lane TMEM shapes), so two
+  // exponential streams of a tile run at once on each sub-partition.
+  static constexpr bool kSplit = HD == 64;
+  static constexpr int kThreads = kSplit ? 640 : 384;
+  // Register split (setmaxnreg): the block launches with kLaunchRegs per
+  // thread; the first warpgroup (producers, MMA issuers) gives registers back
+  // to the softmax warpgroups.
+  static constexpr int kLaunchRegs = kSplit ? 96 : 168;
+  static constexpr uint32_t kRegsCtl = kSplit ? 64 : 88;
+  static constexpr uint32_t kRegsSoftmax = kSplit ? 104 : 208;
+  static_assert(128 * kRegsCtl + (kThreads - 128) * kRegsSoftmax == kThreads * kLaunchRegs,
+                "register split must use the launch budget");
+  static constexpr int kEpiRows = kSplit ? 16 : 32;  // rows of a softmax warp's context box
   static constexpr int kStages = HD == 64 ? 4 : (HD == 128 ? 2 : 1);
   static constexpr int kTileBytes = HD * 2 * 128;  // 128 rows x HD x 2 bytes
   // Q tiles: head_dim 64 double-buffers them (the next item's Q arrives while
@@ -94,7 +103,7 @@ struct AttnSmem {
   // it for each further 64 columns); measured: per-thread 16-byte row stores
   // took 1-2.5K cycles per item end at head_dim 64, ~3.5K at head_dim 128.
   static constexpr int kEpiOff = kVOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kEpiOff + 4 * kNT * 32 * 128;
+  static constexpr int kBarOff = kEpiOff + (kThreads / 32 - 4) * kEpiRows * 128;
   static constexpr int kTotal = 1024 + kBarOff + 512;
   static_assert(kTotal <= 232448, "shared memory budget");
   // TMEM columns
@@ -176,8 +185,231 @@ __device__ __forceinline__ int kv_tiles(int pair, int t, int S) {
   return CAUSAL ? min(NT * pair + 1 + t, total) : total;
 }
 
+// Softmax warps of the head_dim-64 kernel (separate P buffers, two query
+// tiles per item), two per tile on each SM sub-partition: warp w (4..19)
+// serves tile t = (w - 4) / 8 and rows 16 * sub .. 16 * sub + 15 (sub =
+// ((w - 4) / 4) & 1) of TMEM lane quarter w % 4, through the 16-lane TMEM
+// shapes.  Thread lane = 4g + k holds rows g and g + 8 of the warp's 16 and,
+// of each 8-key group n of the key tile, keys 8n + 2k and 8n + 2k + 1; the
+// four threads of a row combine its max and sum with two shuffles.  Per key
+// tile: wait for S, load it, release it (the next S may be computed), mask,
+// row max, P = 2^(s*scale - m) into registers, wait for the previous P.V,
+// store P (P word 4n + k of a row = keys 8n + 2k, 8n + 2k + 1), rescale O when
+// the exponent reference moved, signal.  At an item's end: O / l into a
+// 16-row staging box, one TMA store per warp.
+// Four softmax warps share each sub-partition and run their exponential loops
+// whenever their data is ready.  Measured against one softmax warp per tile
+// and sub-partition (with the two tiles' warps taking turns on the exponential
+// unit): cfg2 shapes non-causal 206.9 -> 194.6 us, B4 S8192 causal 885 -> 797
+// us, B2 S25000 H8 causal 3.43 -> 2.94 ms, cfg2 causal unchanged (127 us);
+// turns between the tiles' warp pairs measured 3-12% slower than none.
+template <typename T, bool CAUSAL>
+__device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_base, uint32_t tmem,
+                                              const CUtensorMap* tm_ctx, uint64_t* s_full, uint64_t* s_free,
+                                              uint64_t* p_full, uint64_t* o_done, volatile int* abort_flag) {
+  using L = AttnSmem<64>;
+  constexpr int NT = L::kNT;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int t = (warp - 4) >> 3;
+  const int sub = ((warp - 4) >> 2) & 1;
+  const int lg = warp & 3;
+  const int g = lane >> 2, kq = lane & 3;
+  const int ra = lg * 32 + sub * 16 + g;  // this thread's rows within the tile: ra, ra + 8
+  const uint32_t t_lane = tmem + (static_cast<uint32_t>(lg * 32 + sub * 16) << 16);
+  const uint32_t t_s = t_lane + t * 128;
+  const uint32_t t_p = t_lane + L::kColP + t * 64;
+  const uint32_t t_o = t_lane + L::kColO + t * 64;
+  uint8_t* box = epi_base + (warp - 4) * (L::kEpiRows * 128);
+  uint32_t sf_phase = 0, od_phase = 0;
+  auto row_max4 = [](float v) {  // max over the four threads of a row
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  };
+  auto row_sum4 = [](float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+  };
+  bool ok = true;
+  for (int k = 0; ok; ++k) {
+    const int item = item_of(k);
+    if (item >= p.num_items) break;
+    const Item it = decode_item<CAUSAL>(item, p);
+    const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
+    const int q0 = it.pair * NT * kBM + t * kBM;
+    const int qa = q0 + ra, qb = qa + 8;
+    const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
+    uint32_t mbyte[4] = {0u, 0u, 0u, 0u};  // lane l: keys l, l+32, l+64, l+96 of the current tile
+    if (kmask != nullptr) {
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) {
+        const int key = gg * 32 + lane;
+        mbyte[gg] = key < p.S ? __ldg(kmask + key) : 0u;
+      }
+    }
+    float m_a = -INFINITY, m_b = -INFINITY;  // exponent references (log2 units), moved lazily
+    float l_a = 0.f, l_b = 0.f;              // this thread's part of each row's sum of P
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait_warp(&s_full[t], sf_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+      sf_phase ^= 1u;
+      tc_fence_after();
+      float s[64];  // s[4n + e]: row (e < 2 ? a : b), key 8n + 2k + (e & 1)
+      {
+        uint32_t u[64];
+        tmem_ld_16x256b_x16(t_s, u);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(u[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);  // the tensor core may overwrite S_t now
+      const int k0 = j * kBN;
+      const bool tail = k0 + kBN > p.S;
+      const bool diag = CAUSAL && k0 + kBN - 1 > q0;
+      uint32_t vbits[4] = {~0u, ~0u, ~0u, ~0u};
+      if (tail || kmask != nullptr) {
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+          const int key = k0 + gg * 32 + lane;
+          bool v = key < p.S;
+          if (kmask != nullptr) v = v && mbyte[gg] != 0u;
+          vbits[gg] = __ballot_sync(0xffffffffu, v);
+        }
+        if (kmask != nullptr && j + 1 < n_kv) {
+#pragma unroll
+          for (int gg = 0; gg < 4; ++gg) {
+            const int key = k0 + kBN + gg * 32 + lane;
+            mbyte[gg] = key < p.S ? __ldg(kmask + key) : 0u;
+          }
+        }
+      }
+      if ((vbits[0] & vbits[1] & vbits[2] & vbits[3]) == ~0u) {
+        if (diag) {  // key k0 + i is visible to row q iff i <= q - k0
+          const int lim_a = qa - k0, lim_b = qb - k0;
+#pragma unroll
+          for (int n = 0; n < 16; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int key = 8 * n + 2 * kq + (e & 1);
+              s[4 * n + e] = key <= (e < 2 ? lim_a : lim_b) ? s[4 * n + e] : -INFINITY;
+            }
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = 8 * n + 2 * kq + (e & 1);
+            bool v = (vbits[key >> 5] >> (key & 31)) & 1u;
+            if (CAUSAL) v = v && (k0 + key <= (e < 2 ? qa : qb));
+            s[4 * n + e] = v ? s[4 * n + e] : -INFINITY;
+          }
+      }
+      // row maxima: four independent chains per row, then the row's four threads
+      float ma[4], mb[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        ma[c] = fmaxf(s[16 * c + 0], s[16 * c + 1]);
+        mb[c] = fmaxf(s[16 * c + 2], s[16 * c + 3]);
+#pragma unroll
+        for (int n = 4 * c + 1; n < 4 * c + 4; ++n) {
+          ma[c] = fmax3(ma[c], s[4 * n], s[4 * n + 1]);
+          mb[c] = fmax3(mb[c], s[4 * n + 2], s[4 * n + 3]);
+        }
+      }
+      const float mxa = row_max4(fmaxf(fmaxf(ma[0], ma[1]), fmaxf(ma[2], ma[3])));
+      const float mxb = row_max4(fmaxf(fmaxf(mb[0], mb[1]), fmaxf(mb[2], mb[3])));
+      // Lazy rescaling as in the other schedules: the reference only moves when
+      // the tile max exceeds it by more than 8 (log2 units).
+      const float mta = mxa * p.scale_log2, mtb = mxb * p.scale_log2;
+      const float mna = (mta > m_a + 8.f) ? mta : m_a;
+      const float mnb = (mtb > m_b + 8.f) ? mtb : m_b;
+      const float mua = mna == -INFINITY ? 0.f : mna;
+      const float mub = mnb == -INFINITY ? 0.f : mnb;
+      const float alpha_a = fast_exp2(m_a - mua);
+      const float alpha_b = fast_exp2(m_b - mub);
+      const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t nma = f2_pack(-mua, -mua), nmb = f2_pack(-mub, -mub);
+      uint32_t pk[32];  // P words: pk[2n] row a, pk[2n + 1] row b, word column 4n + k
+      uint64_t sa2[2] = {0ull, 0ull}, sb2[2] = {0ull, 0ull};
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        float x0, x1;
+        f2_unpack(ffma2(f2_pack(s[4 * n], s[4 * n + 1]), c2, nma), x0, x1);
+        const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+        pk[2 * n] = Pack<T>::two(e0, e1);
+        sa2[n & 1] = fadd2(sa2[n & 1], f2_pack(e0, e1));
+        f2_unpack(ffma2(f2_pack(s[4 * n + 2], s[4 * n + 3]), c2, nmb), x0, x1);
+        const float e2 = fast_exp2(x0), e3 = fast_exp2(x1);
+        pk[2 * n + 1] = Pack<T>::two(e2, e3);
+        sb2[n & 1] = fadd2(sb2[n & 1], f2_pack(e2, e3));
+      }
+      float a0, a1, b0, b1;
+      f2_unpack(fadd2(sa2[0], sa2[1]), a0, a1);
+      f2_unpack(fadd2(sb2[0], sb2[1]), b0, b1);
+      l_a = l_a * alpha_a + (a0 + a1);
+      l_b = l_b * alpha_b + (b0 + b1);
+      m_a = mna;
+      m_b = mnb;
+      if (j > 0) {
+        // P_t(j-1) V must have completed: it reads the P buffer written here and
+        // it is the last write to O_t before a rescale.
+        if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
+        od_phase ^= 1u;
+        tc_fence_after();
+      }
+      tmem_st_16x128b_x16(t_p, pk);
+      if (j > 0 && __any_sync(0xffffffffu, alpha_a != 1.f || alpha_b != 1.f)) {
+        uint32_t o[32];
+        tmem_ld_16x256b_x8(t_o, o);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          o[4 * n + 0] = __float_as_uint(__uint_as_float(o[4 * n + 0]) * alpha_a);
+          o[4 * n + 1] = __float_as_uint(__uint_as_float(o[4 * n + 1]) * alpha_a);
+          o[4 * n + 2] = __float_as_uint(__uint_as_float(o[4 * n + 2]) * alpha_b);
+          o[4 * n + 3] = __float_as_uint(__uint_as_float(o[4 * n + 3]) * alpha_b);
+        }
+        tmem_st_16x256b_x8(t_o, o);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (!ok) break;
+    // epilogue: wait for the last P.V, then O_t / l -> this warp's 16 context rows
+    if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) break;
+    od_phase ^= 1u;
+    tc_fence_after();
+    const float inv_a = 1.f / row_sum4(l_a);
+    const float inv_b = 1.f / row_sum4(l_b);
+    if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
+    __syncwarp();
+    {
+      uint32_t o[32];  // o[4n + e]: row (e < 2 ? a : b), column 8n + 2k + (e & 1)
+      tmem_ld_16x256b_x8(t_o, o);
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        // 128-byte rows, 16-byte chunk n holds columns 8n..8n+7, swizzled by row & 7
+        const uint32_t wa = Pack<T>::two(__uint_as_float(o[4 * n]) * inv_a, __uint_as_float(o[4 * n + 1]) * inv_a);
+        const uint32_t wb = Pack<T>::two(__uint_as_float(o[4 * n + 2]) * inv_b, __uint_as_float(o[4 * n + 3]) * inv_b);
+        *reinterpret_cast<uint32_t*>(box + g * 128 + ((n ^ (g & 7)) << 4) + 4 * kq) = wa;
+        *reinterpret_cast<uint32_t*>(box + (g + 8) * 128 + ((n ^ ((g + 8) & 7)) << 4) + 4 * kq) = wb;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      // rows >= S and columns >= head_dim are clipped by the map
+      tma_store_4d(tm_ctx, box, 0, it.h, q0 + lg * 32 + sub * 16, it.b);
+      bulk_commit_group();
+    }
+    // The next item's first P.V overwrites O_t only after this thread's next
+    // p_full arrival, which follows these TMEM loads.
+  }
+  if (lane == 0) bulk_wait_group_all();  // context stores complete before exit
+}
+
 template <typename T, int HD, bool CAUSAL>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(AttnSmem<HD>::kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_ctx,
                  const AttnParams p) {
   using L = AttnSmem<HD>;
@@ -208,8 +440,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
   uint64_t* p_full = s_free + 2;        // [2] per tile: P_t written
   uint64_t* o_done = p_full + 2;        // [2] per tile: one phase per completed P_t V
   uint64_t* drain = o_done + 2;         // [2] per tile: every MMA of its issuer completed
-  uint64_t* turn = drain + 2;           // [2][4]: tile t's softmax warp on sub-partition q may run its exponentials
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -230,14 +461,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         mbar_init(&q_empty[b * 2 + t], 1);
       }
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 128);
-      mbar_init(&p_full[t], 128);
+      mbar_init(&s_free[t], L::kSplit ? 256 : 128);   // every softmax thread of the tile
+      mbar_init(&p_full[t], L::kSplit ? 256 : 128);
       mbar_init(&o_done[t], 1);
       mbar_init(&drain[t], 1);
-      for (int q = 0; q < 4; ++q) mbar_init(&turn[t * 4 + q], 1);
     }
-    // tile A takes the first turn on every sub-partition
-    for (int q = 0; q < 4; ++q) mbar_arrive(&turn[q]);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -254,7 +482,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
   grid_launch_dependents();
 
   if (warp < 4) {
-    setmaxnreg_dec<kRegsCtl>();
+    setmaxnreg_dec<L::kRegsCtl>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ K/V producer
       // A stage is refilled once every tile that used its previous key tile has
@@ -501,7 +729,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       }
     }
   } else {
-    setmaxnreg_inc<kRegsSoftmax>();
+    setmaxnreg_inc<L::kRegsSoftmax>();
+    if constexpr (L::kSplit) {
+      softmax_split<T, CAUSAL>(p, smem + L::kEpiOff, tmem, &tm_ctx, s_full, s_free, p_full, o_done, abort_flag);
+    } else {
     // ------------------------------------------------------------ softmax (tile A or B)
     const int t = warp >= 8 ? 1 : 0;
     if (t < NT) {  // one tile per item: warps 8..11 have no work
@@ -513,39 +744,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
     const uint32_t t_o = t_lane + L::kColO + t * HD;
     uint32_t sf_phase = 0;
     uint32_t od_phase = 0;  // o_done parity of the next P.V to wait for
-    // Exponential turns (two tiles per item): on each SM sub-partition the two
-    // softmax warps (tile A's and tile B's) run their exponential loops in turn,
-    // so each one's loads, row max and P store proceed while the other one's
-    // exponentials keep the MUFU pipe busy.  Measured: one warp alone drives
-    // the exponential unit at ~84% of its rate, two at ~97%; without turns the
-    // two tiles fall into step (both exponentiate, then both leave the unit
-    // idle).  Turns are taken on an item's interior key tiles only, j in
-    // [1, n_A - 1) for both tiles (n_A = tile A's key-tile count), so both
-    // take the same number and the sequences stay aligned; an item's first and
-    // last steps run free, so a tile waiting for its last P.V or storing its
-    // context never holds up the other tile's exponentials (with turns on every
-    // step, tile A waited ~3,000 cycles per causal item).  Used at head_dim 64
-    // (cfg2 shapes: non-causal 226 -> 214 us, B4 S8192 causal ~5% faster); at
-    // head_dim 128, where the next S of a tile waits for its own P.V, turns
-    // measured 2% slower.
-    constexpr bool kTurns = HD == 64;
-    uint32_t turn_ph = 0;
-    auto take_turn = [&]() -> bool {
-      const bool got = mbar_wait_warp(&turn[t * 4 + lg], turn_ph, p.status, kDevTimeoutSoftmax, abort_flag);
-      turn_ph ^= 1u;
-      return got;
-    };
-    auto pass_turn = [&]() {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + lg]);
-    };
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int item = item_of(k);
       if (item >= p.num_items) break;
       const Item it = decode_item<CAUSAL>(item, p);
       const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
-      const int n_turn_end = kv_tiles<CAUSAL, NT>(it.pair, 0, p.S);  // turns on steps [1, n_A - 1)
       const int q0 = it.pair * NT * kBM + t * kBM;
       const int q_row = q0 + r;
       const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
@@ -649,8 +853,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         // row sums as fp32 pairs in four chains.
         uint32_t pk[2][32];
         uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-        const bool turn_step = kTurns && j >= 1 && j + 1 < n_turn_end;
-        if (turn_step && !take_turn()) { ok = false; break; }
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) {
           uint32_t (&pc)[16] = *reinterpret_cast<uint32_t(*)[16]>(&pk[c >> 1][(c & 1) * 16]);
@@ -666,7 +868,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           }
           if constexpr (!kSepP) tmem_st16(t_p + c * 16, pc);
         }
-        if (turn_step) pass_turn();
         float a0, a1;
         f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), a0, a1);
         const float sum = a0 + a1;
@@ -741,6 +942,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
     }
     if (lane == 0) bulk_wait_group_all();  // context stores complete before exit
     }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -769,7 +971,7 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tm_ctx;
   const uint64_t cdims[4] = {hd, H, (uint64_t)a.seq_len, (uint64_t)a.batch};
   const uint64_t cstrides[3] = {hd * 2, D * 2, (uint64_t)a.seq_len * D * 2};
-  const uint32_t cbox[4] = {64, 1, 32, 1};
+  const uint32_t cbox[4] = {64, 1, (uint32_t)L::kEpiRows, 1};
   rc = encode_tmap(&tm_ctx, dt, 4, a.ctx, cdims, cstrides, cbox);
   if (rc) return rc;
   AttnParams p;
@@ -793,12 +995,12 @@ int launch_attn(const AttnArgs& a, cudaStream_t stream) {
     // with any other the softmax warps' setmaxnreg.inc could never complete.
     cudaFuncAttributes fa;
     TTJ_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
-    if (fa.numRegs != kLaunchRegs)
+    if (fa.numRegs != L::kLaunchRegs)
       return fail(TTJ_ERR_UNSUPPORTED, "attention kernel register count differs from its register split");
   }
   TTJ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
   const int grid = p.num_items < sm_count() ? p.num_items : sm_count();
-  TTJ_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), L::kTotal, stream, tm, tm_ctx, p));
+  TTJ_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(L::kThreads), L::kTotal, stream, tm, tm_ctx, p));
   return TTJ_OK;
 }
 
