@@ -78,7 +78,9 @@ struct AttnSmem {
   static constexpr bool kSepP = HD == 64;           // separate P buffers in TMEM
   // head_dim 64: two softmax warps per tile on each SM sub-partition, each
   // owning 16 of the quarter's 32 rows (16-lane TMEM shapes), so two
-  // exponential streams of a tile run at once on each sub-partition.
+  // exponential streams of a tile run at once on each sub-partition.  (The
+  // same split of the head_dim-128 schedule, P over S, measured 5-22% slower:
+  // B2 S4096 H32 causal 289 -> 351 us, non-causal 466 -> 493 us.)
   static constexpr bool kSplit = HD == 64;
   static constexpr int kThreads = kSplit ? 640 : 384;
   // Register split (setmaxnreg): the block launches with kLaunchRegs per
@@ -203,12 +205,13 @@ __device__ __forceinline__ int kv_tiles(int pair, int t, int S) {
 // unit): cfg2 shapes non-causal 206.9 -> 194.6 us, B4 S8192 causal 885 -> 797
 // us, B2 S25000 H8 causal 3.43 -> 2.94 ms, cfg2 causal unchanged (127 us);
 // turns between the tiles' warp pairs measured 3-12% slower than none.
-template <typename T, bool CAUSAL>
+template <typename T, int HD, bool CAUSAL>
 __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_base, uint32_t tmem,
                                               const CUtensorMap* tm_ctx, uint64_t* s_full, uint64_t* s_free,
                                               uint64_t* p_full, uint64_t* o_done, volatile int* abort_flag) {
-  using L = AttnSmem<64>;
+  using L = AttnSmem<HD>;
   constexpr int NT = L::kNT;
+  constexpr bool kSepP = L::kSepP;  // head_dim 64: separate P buffers; 128: P over S
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int t = (warp - 4) >> 3;
@@ -218,8 +221,8 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
   const int ra = lg * 32 + sub * 16 + g;  // this thread's rows within the tile: ra, ra + 8
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(lg * 32 + sub * 16) << 16);
   const uint32_t t_s = t_lane + t * 128;
-  const uint32_t t_p = t_lane + L::kColP + t * 64;
-  const uint32_t t_o = t_lane + L::kColO + t * 64;
+  const uint32_t t_p = t_lane + L::kColP + t * (kSepP ? 64 : 128);
+  const uint32_t t_o = t_lane + L::kColO + t * HD;
   uint8_t* box = epi_base + (warp - 4) * (L::kEpiRows * 128);
   uint32_t sf_phase = 0, od_phase = 0;
   auto row_max4 = [](float v) {  // max over the four threads of a row
@@ -260,8 +263,10 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
 #pragma unroll
         for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(u[i]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[t]);  // the tensor core may overwrite S_t now
+      if constexpr (kSepP) {
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);  // the tensor core may overwrite S_t now
+      }
       const int k0 = j * kBN;
       const bool tail = k0 + kBN > p.S;
       const bool diag = CAUSAL && k0 + kBN - 1 > q0;
@@ -350,25 +355,29 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
       l_b = l_b * alpha_b + (b0 + b1);
       m_a = mna;
       m_b = mnb;
-      if (j > 0) {
+      if (kSepP && j > 0) {
         // P_t(j-1) V must have completed: it reads the P buffer written here and
-        // it is the last write to O_t before a rescale.
+        // it is the last write to O_t before a rescale.  (With P over S, S_t(j)
+        // being ready already means that P.V has completed.)
         if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
         od_phase ^= 1u;
         tc_fence_after();
       }
-      tmem_st_16x128b_x16(t_p, pk);
+      tmem_st_16x128b_x16(t_p, pk);  // P over S: only this warp's rows, already loaded
       if (j > 0 && __any_sync(0xffffffffu, alpha_a != 1.f || alpha_b != 1.f)) {
-        uint32_t o[32];
-        tmem_ld_16x256b_x8(t_o, o);
+#pragma unroll 1
+        for (int hh = 0; hh < HD / 64; ++hh) {
+          uint32_t o[32];
+          tmem_ld_16x256b_x8(t_o + 64 * hh, o);
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          o[4 * n + 0] = __float_as_uint(__uint_as_float(o[4 * n + 0]) * alpha_a);
-          o[4 * n + 1] = __float_as_uint(__uint_as_float(o[4 * n + 1]) * alpha_a);
-          o[4 * n + 2] = __float_as_uint(__uint_as_float(o[4 * n + 2]) * alpha_b);
-          o[4 * n + 3] = __float_as_uint(__uint_as_float(o[4 * n + 3]) * alpha_b);
+          for (int n = 0; n < 8; ++n) {
+            o[4 * n + 0] = __float_as_uint(__uint_as_float(o[4 * n + 0]) * alpha_a);
+            o[4 * n + 1] = __float_as_uint(__uint_as_float(o[4 * n + 1]) * alpha_a);
+            o[4 * n + 2] = __float_as_uint(__uint_as_float(o[4 * n + 2]) * alpha_b);
+            o[4 * n + 3] = __float_as_uint(__uint_as_float(o[4 * n + 3]) * alpha_b);
+          }
+          tmem_st_16x256b_x8(t_o + 64 * hh, o);
         }
-        tmem_st_16x256b_x8(t_o, o);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -381,11 +390,13 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
     tc_fence_after();
     const float inv_a = 1.f / row_sum4(l_a);
     const float inv_b = 1.f / row_sum4(l_b);
-    if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
-    __syncwarp();
-    {
-      uint32_t o[32];  // o[4n + e]: row (e < 2 ? a : b), column 8n + 2k + (e & 1)
-      tmem_ld_16x256b_x8(t_o, o);
+#pragma unroll 1
+    for (int hh = 0; hh < HD / 64; ++hh) {
+      if (64 * hh >= p.hd) break;  // only zero padding left (uniform)
+      if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
+      __syncwarp();
+      uint32_t o[32];  // o[4n + e]: row (e < 2 ? a : b), column 64hh + 8n + 2k + (e & 1)
+      tmem_ld_16x256b_x8(t_o + 64 * hh, o);
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         // 128-byte rows, 16-byte chunk n holds columns 8n..8n+7, swizzled by row & 7
@@ -394,13 +405,13 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
         *reinterpret_cast<uint32_t*>(box + g * 128 + ((n ^ (g & 7)) << 4) + 4 * kq) = wa;
         *reinterpret_cast<uint32_t*>(box + (g + 8) * 128 + ((n ^ ((g + 8) & 7)) << 4) + 4 * kq) = wb;
       }
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      // rows >= S and columns >= head_dim are clipped by the map
-      tma_store_4d(tm_ctx, box, 0, it.h, q0 + lg * 32 + sub * 16, it.b);
-      bulk_commit_group();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        // rows >= S and columns >= head_dim are clipped by the map
+        tma_store_4d(tm_ctx, box, 64 * hh, it.h, q0 + lg * 32 + sub * 16, it.b);
+        bulk_commit_group();
+      }
     }
     // The next item's first P.V overwrites O_t only after this thread's next
     // p_full arrival, which follows these TMEM loads.
@@ -731,7 +742,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
   } else {
     setmaxnreg_inc<L::kRegsSoftmax>();
     if constexpr (L::kSplit) {
-      softmax_split<T, CAUSAL>(p, smem + L::kEpiOff, tmem, &tm_ctx, s_full, s_free, p_full, o_done, abort_flag);
+      softmax_split<T, HD, CAUSAL>(p, smem + L::kEpiOff, tmem, &tm_ctx, s_full, s_free, p_full, o_done, abort_flag);
     } else {
     // ------------------------------------------------------------ softmax (tile A or B)
     const int t = warp >= 8 ? 1 : 0;
