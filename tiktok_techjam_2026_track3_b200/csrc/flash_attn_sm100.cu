@@ -187,8 +187,9 @@ __device__ __forceinline__ int kv_tiles(int pair, int t, int S) {
   return CAUSAL ? min(NT * pair + 1 + t, total) : total;
 }
 
-// Softmax warps of the head_dim-64 kernel (separate P buffers, two query
-// tiles per item), two per tile on each SM sub-partition: warp w (4..19)
+// Softmax warps, two per query tile on each SM sub-partition (the head_dim-64
+// kernel: separate P buffers, two query tiles per item; the P-over-S layout of
+// head_dim 128 is handled too, but measured slower there): warp w (4..19)
 // serves tile t = (w - 4) / 8 and rows 16 * sub .. 16 * sub + 15 (sub =
 // ((w - 4) / 4) & 1) of TMEM lane quarter w % 4, through the 16-lane TMEM
 // shapes.  Thread lane = 4g + k holds rows g and g + 8 of the warp's 16 and,
