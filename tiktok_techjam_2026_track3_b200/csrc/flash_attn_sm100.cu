@@ -289,15 +289,18 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
         }
       }
       if ((vbits[0] & vbits[1] & vbits[2] & vbits[3]) == ~0u) {
-        if (diag) {  // key k0 + i is visible to row q iff i <= q - k0
-          const int lim_a = qa - k0, lim_b = qb - k0;
+        if (diag) {
+          // key k0 + 8n + 2k + (e & 1) is visible to row q iff 8n + (e & 1) <=
+          // q - k0 - 2k: one compare with a constant per score (measured: cfg2
+          // causal 131.1 -> 129.0 us against computing each key's index)
+          const int da = qa - k0 - 2 * kq, db = qb - k0 - 2 * kq;
 #pragma unroll
-          for (int n = 0; n < 16; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int key = 8 * n + 2 * kq + (e & 1);
-              s[4 * n + e] = key <= (e < 2 ? lim_a : lim_b) ? s[4 * n + e] : -INFINITY;
-            }
+          for (int n = 0; n < 16; ++n) {
+            s[4 * n + 0] = 8 * n <= da ? s[4 * n + 0] : -INFINITY;
+            s[4 * n + 1] = 8 * n + 1 <= da ? s[4 * n + 1] : -INFINITY;
+            s[4 * n + 2] = 8 * n <= db ? s[4 * n + 2] : -INFINITY;
+            s[4 * n + 3] = 8 * n + 1 <= db ? s[4 * n + 3] : -INFINITY;
+          }
         }
       } else {
 #pragma unroll
