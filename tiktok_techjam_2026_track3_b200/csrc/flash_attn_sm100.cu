@@ -749,6 +749,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
       softmax_split<T, HD, CAUSAL>(p, smem + L::kEpiOff, tmem, &tm_ctx, s_full, s_free, p_full, o_done, abort_flag);
     } else {
     // ------------------------------------------------------------ softmax (tile A or B)
+    // One warp per tile and TMEM lane quarter, P written over S (head_dim 128 / 256).
+    static_assert(!kSepP, "separate-P schedules use softmax_split");
     const int t = warp >= 8 ? 1 : 0;
     if (t < NT) {  // one tile per item: warps 8..11 have no work
     const int lg = warp & 3;             // TMEM lane quarter of this warp
@@ -790,10 +792,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           tmem_ld128(t_s, u);
 #pragma unroll
           for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(u[i]);
-        }
-        if constexpr (kSepP) {
-          tc_fence_before();
-          mbar_arrive(&s_free[t]);  // the tensor core may overwrite S_t now
         }
         const int k0 = j * kBN;
         // Which of the tile's 128 keys this row may see: keys past S, keys the
@@ -858,9 +856,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         const float m_new = (m_tile > m_run + 8.f) ? m_tile : m_run;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
         const float alpha = fast_exp2(m_run - m_use);  // 1 unchanged, 0 from -inf
-        // x = s * scale_log2 - m as packed pairs; P = 2^x.  Written over the S
-        // columns already read 16 columns (32 keys) at a time, or, with separate
-        // P buffers, kept in registers and stored after the wait below.
+        // x = s * scale_log2 - m as packed pairs; P = 2^x, written over the S
+        // columns already read 16 columns (32 keys) at a time.
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
         const uint64_t nm2 = f2_pack(-m_use, -m_use);
         // One MUFU exponential per element in fp32 (measured faster than the
@@ -881,25 +878,13 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
             pc[ii] = Pack<T>::two(e0, e1);
             sum2[i & 3] = fadd2(sum2[i & 3], f2_pack(e0, e1));
           }
-          if constexpr (!kSepP) tmem_st16(t_p + c * 16, pc);
+          tmem_st16(t_p + c * 16, pc);  // over the S columns already read
         }
         float a0, a1;
         f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), a0, a1);
         const float sum = a0 + a1;
         l_run = l_run * alpha + sum;
         m_run = m_new;
-        if constexpr (kSepP) {
-          if (j > 0) {
-            // P_t(j-1) V must have completed: it reads the P buffer written here
-            // and it is the last write to O_t before a rescale.  It was issued a
-            // whole softmax step ago, so this wait is normally free.
-            if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) { ok = false; break; }
-            od_phase ^= 1u;
-            tc_fence_after();
-          }
-          tmem_st32(t_p, pk[0]);
-          tmem_st32(t_p + 32, pk[1]);
-        }
         // Rescale O_t when the exponent reference moved (O_t holds P(0..j-1) V).
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
