@@ -1065,6 +1065,8 @@ def main():
         cfg = cfg.with_(batch=args.batch)
     if args.seq:
         cfg = cfg.with_(seq_len=args.seq)
+    if args.batch or args.seq:  # the workload name says what actually ran
+        cfg = cfg.with_(name=f"{PRESETS[args.config].name} (overridden: batch {cfg.batch}, seq_len {cfg.seq_len})")
     if args.impl == "reference":
         return run_reference(args, cfg)
     if args.block:
