@@ -24,7 +24,10 @@ def _rand(shape, g, scale, dtype):
 
 
 SHAPES = [(128, 256, 64), (200, 96, 72), (1, 32, 8), (1000, 768, 256), (777, 512, 1000),
-          (4096, 3072, 1024), (2048, 1024, 4096)]
+          (4096, 3072, 1024), (2048, 1024, 4096),
+          # more 256 x 256 tiles than CTA pairs, the last partial wave small enough to run as
+          # 256 x 128 column halves (80 tiles on 74 pairs: 6 tiles -> 12 halves), ragged rows
+          (10163, 512, 320)]
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
@@ -45,7 +48,9 @@ def test_linear_bias(dt, m, n, k):
                                    # more tiles than CTA pairs (or CTAs), last row block ragged:
                                    # an epilogue warp requests its next tile's first residual box
                                    # before that tile's accumulator is ready
-                                   (16461, 1024, 256), (16400, 256, 128), (64, 40960, 64)])
+                                   (16461, 1024, 256), (16400, 256, 128), (64, 40960, 64),
+                                   # tail tiles as column halves (see SHAPES)
+                                   (10163, 512, 320), (16384, 1024, 1024)])
 def test_linear_residual_rowmask(dt, m, n, k):
     g = torch.Generator().manual_seed(11)
     x, w = _rand((m, k), g, 1.0, DT[dt]), _rand((n, k), g, k ** -0.5, DT[dt])
@@ -77,7 +82,7 @@ def test_quant_rows_bit_exact(dt):
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 128), (300, 96, 160), (1, 32, 16), (2048, 1536, 4096),
-                                   (4096, 4096, 4096)])
+                                   (4096, 4096, 4096), (10163, 512, 320)])
 def test_int8_gemm_s32_bit_exact(m, n, k):
     g = torch.Generator().manual_seed(m + n + k)
     a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8).cuda()
@@ -88,7 +93,7 @@ def test_int8_gemm_s32_bit_exact(m, n, k):
 
 
 @pytest.mark.parametrize("out", ["bf16", "fp16"])
-@pytest.mark.parametrize("m,n,k", [(513, 768, 256), (4096, 3072, 1024)])
+@pytest.mark.parametrize("m,n,k", [(513, 768, 256), (4096, 3072, 1024), (10163, 512, 320)])
 def test_int8_linear_dequant(out, m, n, k):
     """Dequant epilogue follows the recipe's op order, so it is bit-exact in
     fp32 and therefore after rounding to the output dtype."""
