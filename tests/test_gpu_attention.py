@@ -80,6 +80,21 @@ def test_flash_matches_dense(dt, B, S, H, hd, causal):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B,S,H,hd,causal", [(2, 2048, 8, 256, True), (4, 2048, 8, 256, True),
+                                             (4, 2048, 8, 256, False), (4, 2048, 8, 128, True),
+                                             (3, 4096, 8, 64, True)])
+def test_flash_several_items_per_cta(dt, B, S, H, hd, causal):
+    """More work items than the 148 persistent CTAs (256 to 512 items), so a CTA
+    runs up to 4 items back to back and its K/V producer, MMA issuer and
+    softmax warps must agree on every item's number of key tiles across item
+    boundaries (head_dim 256: one query tile per item and a single K/V stage)."""
+    qkv = make_qkv(B, S, H, hd, dt, 4242 + S + hd)
+    ctx = ops.flash_attn(qkv, H, causal)
+    ops.check_device_status(qkv.device)
+    check_ctx(qkv, H, causal, ctx)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
 @pytest.mark.parametrize("kind", ["prefix", "random"])
 @pytest.mark.parametrize("B,S,H,hd,causal", [(3, 200, 2, 64, True), (2, 300, 2, 128, False),
                                              (2, 1024, 4, 64, True), (3, 128, 4, 32, True),

@@ -87,8 +87,10 @@ struct AttnSmem {
   // thread; the first warpgroup (producers, MMA issuers) gives registers back
   // to the softmax warpgroups.
   static constexpr int kLaunchRegs = kSplit ? 96 : 168;
-  static constexpr uint32_t kRegsCtl = kSplit ? 64 : 88;
-  static constexpr uint32_t kRegsSoftmax = kSplit ? 104 : 208;
+  // (136 / 184: the smallest control share whose producer and MMA-issuer code
+  // compiles without spills at head_dim 128 and 256.)
+  static constexpr uint32_t kRegsCtl = kSplit ? 64 : 136;
+  static constexpr uint32_t kRegsSoftmax = kSplit ? 104 : 184;
   static_assert(128 * kRegsCtl + (kThreads - 128) * kRegsSoftmax == kThreads * kLaunchRegs,
                 "register split must use the launch budget");
   static constexpr int kEpiRows = kSplit ? 16 : 32;  // rows of a softmax warp's context box
@@ -525,7 +527,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
         if (item >= p.num_items) break;
         const Item it = decode_item<CAUSAL>(item, p);
         const int n_a = kv_tiles<CAUSAL, NT>(it.pair, 0, p.S);
-        const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, 1, p.S);
+        // key tiles of the item's last tile (with one tile per item, tile A's)
+        const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, NT - 1, p.S);
         const int yk = p.H + it.h, yv = 2 * p.H + it.h;  // head index of K / V in the 3H axis
         for (int j = 0; j < n_kv; ++j, ++kv) {
           const int st = kv % ST;
@@ -598,7 +601,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           if (item >= p.num_items) return false;
           const Item it = decode_item<CAUSAL>(item, p);
           qk_n = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
-          qk_nb = kv_tiles<CAUSAL, NT>(it.pair, 1, p.S);
+          qk_nb = kv_tiles<CAUSAL, NT>(it.pair, NT - 1, p.S);
           return true;
         };
         bool qk_live = qk_open();
@@ -637,7 +640,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__
           if (item >= p.num_items) break;
           const Item it = decode_item<CAUSAL>(item, p);
           const int n = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
-          const int n_b = kv_tiles<CAUSAL, NT>(it.pair, 1, p.S);
+          const int n_b = kv_tiles<CAUSAL, NT>(it.pair, NT - 1, p.S);
           for (int j = 0; j < n; ++j) {
             // S_t(j+1), or the next item's S_t(0) (its Q is double-buffered, so
             // normally already loaded), then this key tile's P.V.  Issuing the
