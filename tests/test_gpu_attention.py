@@ -82,12 +82,15 @@ def test_flash_matches_dense(dt, B, S, H, hd, causal):
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
 @pytest.mark.parametrize("B,S,H,hd,causal", [(2, 2048, 8, 256, True), (4, 2048, 8, 256, True),
                                              (4, 2048, 8, 256, False), (4, 2048, 8, 128, True),
-                                             (3, 4096, 8, 64, True)])
+                                             (3, 4096, 8, 64, True), (2000, 128, 4, 32, True),
+                                             (600, 200, 2, 128, True), (300, 300, 2, 256, True)])
 def test_flash_several_items_per_cta(dt, B, S, H, hd, causal):
-    """More work items than the 148 persistent CTAs (256 to 512 items), so a CTA
-    runs up to 4 items back to back and its K/V producer, MMA issuer and
+    """More work items than the 148 persistent CTAs (256 to 8000 items), so a CTA
+    runs up to 55 items back to back and its K/V producer, MMA issuer and
     softmax warps must agree on every item's number of key tiles across item
-    boundaries (head_dim 256: one query tile per item and a single K/V stage)."""
+    boundaries (head_dim 256: one query tile per item and a single K/V stage;
+    the large-batch cases are official shape 6's form, B=10000 S=128 head_dim 32,
+    at a fifth of its batch, and ragged S with one or three key tiles)."""
     qkv = make_qkv(B, S, H, hd, dt, 4242 + S + hd)
     ctx = ops.flash_attn(qkv, H, causal)
     ops.check_device_status(qkv.device)
@@ -98,7 +101,8 @@ def test_flash_several_items_per_cta(dt, B, S, H, hd, causal):
 @pytest.mark.parametrize("kind", ["prefix", "random"])
 @pytest.mark.parametrize("B,S,H,hd,causal", [(3, 200, 2, 64, True), (2, 300, 2, 128, False),
                                              (2, 1024, 4, 64, True), (3, 128, 4, 32, True),
-                                             (2, 400, 2, 256, True)])
+                                             (2, 400, 2, 256, True), (64, 300, 4, 64, True),
+                                             (40, 200, 4, 128, False), (40, 300, 4, 256, True)])
 def test_flash_key_mask(dt, kind, B, S, H, hd, causal):
     qkv = make_qkv(B, S, H, hd, dt, 77 + S)
     g = torch.Generator().manual_seed(S)
