@@ -226,7 +226,8 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
   const uint32_t t_s = t_lane + t * 128;
   const uint32_t t_p = t_lane + L::kColP + t * (kSepP ? 64 : 128);
   const uint32_t t_o = t_lane + L::kColO + t * HD;
-  uint8_t* box = epi_base + (warp - 4) * (L::kEpiRows * 128);
+  // this warp's context staging box, as a shared-memory address
+  const uint32_t box = smem_u32(epi_base) + (warp - 4) * (L::kEpiRows * 128);
   uint32_t sf_phase = 0, od_phase = 0;
   auto row_max4 = [](float v) {  // max over the four threads of a row
     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
@@ -244,13 +245,19 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
     const int n_kv = kv_tiles<CAUSAL, NT>(it.pair, t, p.S);
     const int q0 = it.pair * NT * kBM + t * kBM;
     const int qa = q0 + ra, qb = qa + 8;
-    const uint8_t* kmask = p.key_mask != nullptr ? p.key_mask + (int64_t)it.b * p.S : nullptr;
-    uint32_t mbyte[4] = {0u, 0u, 0u, 0u};  // lane l: keys l, l+32, l+64, l+96 of the current tile
-    if (kmask != nullptr) {
+    const bool has_mask = p.key_mask != nullptr;
+    const uint8_t* kmask = has_mask ? p.key_mask + (int64_t)it.b * p.S : nullptr;
+    // bit gg: key gg * 32 + lane of the current key tile is valid (one register
+    // for the lane's four keys; with fewer registers held across the loop the
+    // causal kernel compiles without spills: cfg2 causal 129.0 -> 126.0 us,
+    // non-causal 205.8 -> 199.7 us together with the 32-bit box address and
+    // 1 / l taken before the last P.V wait, same output bits)
+    uint32_t mbits = 0u;
+    if (has_mask) {
 #pragma unroll
       for (int gg = 0; gg < 4; ++gg) {
         const int key = gg * 32 + lane;
-        mbyte[gg] = key < p.S ? __ldg(kmask + key) : 0u;
+        mbits |= (key < p.S && __ldg(kmask + key) != 0) ? 1u << gg : 0u;
       }
     }
     float m_a = -INFINITY, m_b = -INFINITY;  // exponent references (log2 units), moved lazily
@@ -274,19 +281,20 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
       const bool tail = k0 + kBN > p.S;
       const bool diag = CAUSAL && k0 + kBN - 1 > q0;
       uint32_t vbits[4] = {~0u, ~0u, ~0u, ~0u};
-      if (tail || kmask != nullptr) {
+      if (tail || has_mask) {
 #pragma unroll
         for (int gg = 0; gg < 4; ++gg) {
           const int key = k0 + gg * 32 + lane;
           bool v = key < p.S;
-          if (kmask != nullptr) v = v && mbyte[gg] != 0u;
+          if (has_mask) v = v && ((mbits >> gg) & 1u);
           vbits[gg] = __ballot_sync(0xffffffffu, v);
         }
-        if (kmask != nullptr && j + 1 < n_kv) {
+        if (has_mask && j + 1 < n_kv) {  // the next tile's bits
+          mbits = 0u;
 #pragma unroll
           for (int gg = 0; gg < 4; ++gg) {
             const int key = k0 + kBN + gg * 32 + lane;
-            mbyte[gg] = key < p.S ? __ldg(kmask + key) : 0u;
+            mbits |= (key < p.S && __ldg(kmask + key) != 0) ? 1u << gg : 0u;
           }
         }
       }
@@ -309,8 +317,9 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
         for (int n = 0; n < 16; ++n)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
+            // keys 8n .. 8n + 7 lie in word n / 4 of vbits
             const int key = 8 * n + 2 * kq + (e & 1);
-            bool v = (vbits[key >> 5] >> (key & 31)) & 1u;
+            bool v = (vbits[n >> 2] >> (8 * (n & 3) + 2 * kq + (e & 1))) & 1u;
             if (CAUSAL) v = v && (k0 + key <= (e < 2 ? qa : qb));
             s[4 * n + e] = v ? s[4 * n + e] : -INFINITY;
           }
@@ -390,12 +399,12 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
       mbar_arrive(&p_full[t]);
     }
     if (!ok) break;
-    // epilogue: wait for the last P.V, then O_t / l -> this warp's 16 context rows
+    // epilogue: 1 / l, wait for the last P.V, then O_t / l -> this warp's 16 context rows
+    const float inv_a = 1.f / row_sum4(l_a);
+    const float inv_b = 1.f / row_sum4(l_b);
     if (!mbar_wait_warp(&o_done[t], od_phase, p.status, kDevTimeoutSoftmax, abort_flag)) break;
     od_phase ^= 1u;
     tc_fence_after();
-    const float inv_a = 1.f / row_sum4(l_a);
-    const float inv_b = 1.f / row_sum4(l_b);
 #pragma unroll 1
     for (int hh = 0; hh < HD / 64; ++hh) {
       if (64 * hh >= p.hd) break;  // only zero padding left (uniform)
@@ -408,8 +417,8 @@ __device__ __forceinline__ void softmax_split(const AttnParams& p, uint8_t* epi_
         // 128-byte rows, 16-byte chunk n holds columns 8n..8n+7, swizzled by row & 7
         const uint32_t wa = Pack<T>::two(__uint_as_float(o[4 * n]) * inv_a, __uint_as_float(o[4 * n + 1]) * inv_a);
         const uint32_t wb = Pack<T>::two(__uint_as_float(o[4 * n + 2]) * inv_b, __uint_as_float(o[4 * n + 3]) * inv_b);
-        *reinterpret_cast<uint32_t*>(box + g * 128 + ((n ^ (g & 7)) << 4) + 4 * kq) = wa;
-        *reinterpret_cast<uint32_t*>(box + (g + 8) * 128 + ((n ^ ((g + 8) & 7)) << 4) + 4 * kq) = wb;
+        st_shared_u32(box + g * 128 + ((n ^ (g & 7)) << 4) + 4 * kq, wa);
+        st_shared_u32(box + (g + 8) * 128 + ((n ^ ((g + 8) & 7)) << 4) + 4 * kq, wb);
       }
       fence_proxy_async_smem();
       __syncwarp();

@@ -192,11 +192,21 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                : "memory");
 }
 
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int32_t x, int32_t y,
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src_smem, int32_t x, int32_t y,
                                              int32_t z, int32_t w) {
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
-               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src_smem), "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int32_t x, int32_t y,
+                                             int32_t z, int32_t w) {
+  tma_store_4d(map, smem_u32(src), x, y, z, w);
+}
+
+// 32-bit store to a shared-memory address (a 32-bit register instead of a
+// 64-bit generic pointer held across the softmax loop).
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void bulk_commit_group() {
