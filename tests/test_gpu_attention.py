@@ -102,7 +102,8 @@ def test_flash_several_items_per_cta(dt, B, S, H, hd, causal):
 @pytest.mark.parametrize("B,S,H,hd,causal", [(3, 200, 2, 64, True), (2, 300, 2, 128, False),
                                              (2, 1024, 4, 64, True), (3, 128, 4, 32, True),
                                              (2, 400, 2, 256, True), (64, 300, 4, 64, True),
-                                             (40, 200, 4, 128, False), (40, 300, 4, 256, True)])
+                                             (40, 200, 4, 128, False), (40, 300, 4, 256, True),
+                                             (2, 333, 2, 64, False), (3, 777, 4, 40, False)])
 def test_flash_key_mask(dt, kind, B, S, H, hd, causal):
     qkv = make_qkv(B, S, H, hd, dt, 77 + S)
     g = torch.Generator().manual_seed(S)
